@@ -1,0 +1,257 @@
+/*
+ * nabla_b200.h -- C ABI of the B200 tape-replay engine (libnabla_b200.so).
+ *
+ * This is the boundary a NablaTensor host binds through the Panama FFM API
+ * (java.lang.foreign) to serve engine name "cuda": plain C types, borrowed
+ * host pointers, no exceptions across the ABI, every call returns 0 or a
+ * negative NT_E_* status with a thread-local message from nt_last_error().
+ *
+ * Paths in the "replaces" notes are relative to the reference project root.
+ *
+ * Ownership: host arrays passed in are borrowed for the duration of the call
+ * and copied; every device allocation is owned by an nt_exec and released by
+ * nt_destroy.  An nt_exec is internally serialised (one mutex), so any host
+ * thread may call it; it binds its device on every call.
+ */
+#ifndef NABLA_B200_H
+#define NABLA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NT_ABI_VERSION 1
+
+/* Status codes. */
+#define NT_OK 0
+#define NT_E_INVALID_ARG (-1)  /* bad pointer/size/argument (IllegalArgumentException) */
+#define NT_E_TAPE (-2)         /* malformed tape */
+#define NT_E_UNSUPPORTED (-3)  /* tape/options this engine declines (UnsupportedOperationException) */
+#define NT_E_CUDA (-4)         /* CUDA runtime/driver failure */
+#define NT_E_NVRTC (-5)        /* run-time compilation failure */
+#define NT_E_NCCL (-6)         /* collective failure or timeout */
+#define NT_E_OOM (-7)          /* device allocation failed */
+#define NT_E_STATE (-8)        /* call not valid in the current state (IllegalStateException) */
+#define NT_E_INTERNAL (-9)
+
+/* Op codes: the ordinal order of AadOpEnum
+ * (nablatensor-core/src/main/java/com/nablatensor/engine/AadOpEnum.java:19-50). */
+enum nt_op {
+  NT_CONST = 0, NT_INPUT = 1, NT_RANDN = 2, NT_RANDU = 3, NT_ADD = 4, NT_SUB = 5, NT_MUL = 6,
+  NT_DIV = 7, NT_NEG = 8, NT_EXP = 9, NT_LOG = 10, NT_SQRT = 11, NT_MAX = 12, NT_MIN = 13,
+  NT_ABS = 14
+};
+
+/* Precision: the ordinal order of AadOptions.PrecisionEnum
+ * (nablatensor-core/.../engine/AadOptions.java, FLOAT32 then FLOAT64). */
+enum nt_precision { NT_FLOAT32 = 0, NT_FLOAT64 = 1 };
+
+/*
+ * A recorded tape as flat arrays: the FlatTape layout
+ * (nablatensor-core/.../engine/FlatTape.java:37-79) plus the random-stream
+ * counts of AadTape (AadTape.java:128-196).
+ *   op[i], arg_a[i], arg_b[i], constant[i] for node i in recording order;
+ *   INPUT: arg_a = input index; RANDN/RANDU: arg_a = ordinal within
+ *   (stream, kind), arg_b = stream; unused arguments are -1.
+ * normal_count/uniform_count may be NULL (derived from the nodes).
+ */
+typedef struct nt_tape {
+  int32_t n;
+  const int32_t* op;
+  const int32_t* arg_a;
+  const int32_t* arg_b;
+  const double* constant;
+  int32_t n_in;
+  const int32_t* input_node;
+  int32_t n_out;
+  const int32_t* output_node;
+  int32_t n_streams;
+  const int32_t* normal_count;
+  const int32_t* uniform_count;
+} nt_tape;
+
+/* Option flags. */
+#define NT_FLAG_NO_LOOP 0x1      /* emit straight-line code even when the tape has a step loop */
+#define NT_FLAG_GLOBAL_CKPT 0x2  /* keep step checkpoints in global memory instead of shared memory */
+#define NT_FLAG_NO_DISK_CACHE 0x4
+
+/*
+ * Compile options: AadOptions (AadOptions.java:42-156) plus the engine knobs a
+ * caller may pass through AadOptions.engineOptions("cuda").  Zero means
+ * "choose automatically" for every tuning field.
+ */
+typedef struct nt_options {
+  int32_t precision;   /* NT_FLOAT32 or NT_FLOAT64 */
+  int32_t adjoints;    /* 1: value + adjoints of every input; 0: value only */
+  int32_t device;      /* CUDA device ordinal */
+  int32_t block;       /* threads per block */
+  int32_t seg_units;   /* loop units per checkpoint segment */
+  int32_t min_blocks;  /* __launch_bounds__ minimum blocks per SM */
+  int32_t max_regs;    /* register cap per thread */
+  int32_t flags;       /* NT_FLAG_* */
+} nt_options;
+
+typedef struct nt_exec nt_exec;
+
+/* Kernel statistics (the -Dnablatensor.cuda.kernelStats idea,
+ * nablatensor-engine-cuda/.../backend/cuda/CudaRuntime.java:584-593). */
+typedef struct nt_exec_info {
+  int32_t registers;        /* per thread */
+  int32_t local_bytes;      /* per thread; 0 means no spill */
+  int32_t static_smem;      /* bytes per block */
+  int32_t dynamic_smem;     /* bytes per block (step checkpoints) */
+  int32_t block;            /* threads per block */
+  int32_t blocks_per_sm;    /* resident blocks per SM at this configuration */
+  int32_t grid;             /* persistent grid size */
+  int32_t sm_count;
+  int32_t channels;         /* accumulators: n_out * (2 + n_in) */
+  int32_t loop_start;       /* first node of the step loop, -1 when none */
+  int32_t loop_unit;        /* nodes per loop unit */
+  int32_t loop_units;       /* number of loop units */
+  int32_t steps_per_unit;   /* tape iterations folded into one unit */
+  int32_t seg_units;        /* units per checkpoint segment */
+  int32_t segments;
+  int32_t ckpt_slots;       /* checkpointed values per segment boundary */
+  int32_t stored_per_unit;  /* values kept per unit for the reverse sweep */
+  int32_t ckpt_global;      /* 1 when checkpoints live in global memory */
+  double compile_seconds;   /* NVRTC + module load, 0 on a cache hit */
+  double fwd_flops;         /* algorithmic flops per scenario, forward (weights in DESIGN) */
+  double rev_flops;         /* algorithmic flops per scenario, reverse */
+} nt_exec_info;
+
+/* ABI version (NT_ABI_VERSION of the built library). */
+int nt_version(void);
+
+/* Last error message of the calling thread ("" when none). */
+const char* nt_last_error(void);
+
+/* Device discovery; never faults.  Replaces CudaAadEngine.isAvailable()
+ * (nablatensor-engine-cuda/.../engine/CudaAadEngine.java) and the context set-up
+ * in CudaRuntime.initContext (CudaRuntime.java:206-212). */
+int nt_init(int32_t* n_devices);
+
+/* Validates the tape, emits the sm_100a replay kernel, compiles it with NVRTC
+ * (cached by source hash) and allocates the executable's device state.
+ * Replaces AadEngine.compile (nablatensor-core/.../engine/AadEngine.java:28-48)
+ * as implemented by CudaAadEngine.compile (CudaAadEngine.java:60-73) and
+ * DeviceAadExecutable.compile (DeviceAadExecutable.java:107-119). */
+int nt_compile(const nt_tape* tape, const nt_options* options, nt_exec** out);
+
+/* Binds all n input values (input order); re-pricing never recompiles.
+ * Replaces AadExecutable.setInput (AbstractAadExecutable.java:86-92,
+ * DeviceAadExecutable.java:134-137). */
+int nt_set_inputs(nt_exec* exec, const double* inputs, int32_t n);
+
+/*
+ * One dispatch over `paths` scenarios starting at `path_offset`.
+ * sums receives n_out * (2 + n_in) doubles, per output o:
+ *   [sum v, sum v^2, sum dv/din_0, ..., sum dv/din_{n_in-1}]
+ * (the caller divides by `paths` and forms the standard error as
+ * AadTotals.toResult does, AadTotals.java:68-89).  seconds (may be NULL)
+ * receives the wall time of launch + synchronise + read-back.
+ * Replaces AadExecutable.replay (AadExecutable.java:46-47) as implemented by
+ * DeviceAadExecutable.replay (DeviceAadExecutable.java:140-168).
+ */
+int nt_replay(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed, double* sums,
+              double* seconds);
+
+/*
+ * Device-resident accumulation for long runs (the many-chunk replaySafe of
+ * AbstractAadExecutable.java:101-121 without a read-back per chunk):
+ * nt_replay_accumulate enqueues one dispatch that ADDS its sums into the
+ * executable's device accumulator and returns without waiting;
+ * nt_accumulator_read waits, copies the accumulator to `sums` and, when
+ * reset != 0, zeroes it.
+ */
+int nt_replay_accumulate(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed);
+int nt_accumulator_read(nt_exec* exec, double* sums, int32_t reset);
+
+/* The CUDA stream (cudaStream_t) every launch of this executable goes to. */
+int nt_exec_stream(nt_exec* exec, void** stream);
+
+/* Kernel statistics and plan of the compiled executable. */
+int nt_exec_info_get(nt_exec* exec, nt_exec_info* info);
+
+/* The generated CUDA C source (NUL-terminated, truncated to cap).  *len gets
+ * the full length. */
+int nt_exec_source(nt_exec* exec, char* buf, size_t cap, size_t* len);
+
+/*
+ * Emits the replay source without compiling or touching a GPU.
+ * target 0: the CUDA C that nt_compile hands to NVRTC;
+ * target 1: the same scenario code as host C++ with an
+ *   extern "C" void nt_host_replay(const double* inputs, uint64_t paths,
+ *                                  uint64_t path_offset, uint64_t seed,
+ *                                  double* sums)
+ *   entry point (paths in order, sums in nt_replay's layout); it includes
+ *   nt_device_rt.cuh and must be compiled with -DNT_HOST.
+ */
+int nt_emit_source(const nt_tape* tape, const nt_options* options, int32_t target, char* buf,
+                   size_t cap, size_t* len);
+
+/* Compiles a source emitted for target 0 with NVRTC to an sm_100a cubin
+ * (no GPU needed); *cubin_bytes gets the image size. */
+int nt_nvrtc_check(const char* source, size_t* cubin_bytes);
+
+/* Releases the executable (AadExecutable.close). NULL is a no-op. */
+void nt_destroy(nt_exec* exec);
+
+/* ---- multi-GPU: scenario-range sharding + one NCCL all-reduce ------------- */
+
+/* 128-byte NCCL unique id for rank 0 to broadcast. */
+int nt_dist_unique_id(uint8_t id[128]);
+
+/* Joins this executable to an nranks-wide NCCL communicator (one rank per
+ * GPU, one process per rank).  timeout_ms bounds the join; on expiry the
+ * communicator is aborted and NT_E_NCCL returned. */
+int nt_dist_attach(nt_exec* exec, int32_t nranks, int32_t rank, const uint8_t id[128],
+                   int32_t timeout_ms);
+
+/*
+ * Replays the global scenario range [path_offset, path_offset + total_paths)
+ * with this rank's contiguous shard, then all-reduces the sums vector
+ * (n_out * (2 + n_in) doubles) with one ncclAllReduce.  Every rank receives
+ * the global sums.  chunk_paths > 0 splits this rank's shard into dispatches
+ * of at most that many scenarios, accumulated on the device.
+ * seconds (may be NULL) gets this rank's wall time of the call.
+ */
+int nt_replay_sharded(nt_exec* exec, uint64_t total_paths, uint64_t path_offset, uint64_t seed,
+                      uint64_t chunk_paths, double* sums, double* seconds);
+
+/* Enqueue-only variant for device timing: the shard dispatches plus the
+ * all-reduce go to the executable's stream; results land in the device
+ * accumulator (read with nt_accumulator_read). */
+int nt_replay_sharded_async(nt_exec* exec, uint64_t total_paths, uint64_t path_offset,
+                            uint64_t seed, uint64_t chunk_paths);
+
+/* Leaves the communicator (ncclCommDestroy). */
+int nt_dist_detach(nt_exec* exec);
+
+/* The contiguous shard of [path_offset, path_offset + total_paths) that rank
+ * `rank` of `nranks` replays: the first total % nranks ranks take one extra
+ * path.  Host arithmetic only (no device needed); nt_replay_sharded uses it. */
+int nt_shard_range(uint64_t total_paths, uint64_t path_offset, int32_t nranks, int32_t rank, uint64_t* from,
+                   uint64_t* count);
+
+/* ---- generator known-answer access (tests) -------------------------------- */
+
+/*
+ * Runs the device generator and copies its raw uint32 words to the host:
+ * for p in [0, n_paths), q in [0, n_pairs):
+ *   out[(p * n_pairs + q) * 2 + {0,1}] = Philox words of normal pair
+ *   (pair0 + q) of (path0 + p, seed, stream).
+ * normals (may be NULL) receives the fp64 Box-Muller legs in the same layout.
+ * This is Philox.normal() of nablatensor-engine-cpu/.../cpu/Philox.java:56-78
+ * evaluated on the GPU.
+ */
+int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
+                    uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NABLA_B200_H */

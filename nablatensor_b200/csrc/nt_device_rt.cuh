@@ -1,0 +1,286 @@
+/*
+ * nt_device_rt.cuh -- device runtime shared by every replay kernel.
+ *
+ * One source, three consumers:
+ *   - NVRTC: the emitter hands this file to nvrtcCreateProgram as a named
+ *     header, so every generated sm_100a replay kernel includes it;
+ *   - nvcc: nt_kat.cu includes it for the known-answer kernels that expose
+ *     the raw generator words to the tests;
+ *   - g++ (NT_HOST defined): the emitter's host target, used by the CPU tests
+ *     to check the emitted scenario code against the oracle bit for bit.
+ *
+ * Contents:
+ *   - Philox2x32-10 keyed per (path, seed, stream) exactly as the reference's
+ *     `cpu` engine keys it (nablatensor-engine-cpu/.../cpu/Philox.java:41-95):
+ *       lo = (u32)path ^ (u32)seed, hi = (u32)(path>>32) ^ (u32)(seed>>32),
+ *       stream s != 0: hi ^= s * 0x9E3779B1;
+ *       normal pair c: counter (lo, hi ^ c), key 0x1BD11BDA, 10 rounds of
+ *       (H, L) = 0xD256D193 * x0; x0 = H ^ key ^ x1; x1 = L; key += 0x9E3779B9;
+ *       uniform k: counter (lo, hi ^ (k | 0x40000000)).
+ *   - Box-Muller computing BOTH legs of a pair once (the reference device
+ *     generator recomputes the whole pair per draw,
+ *     nablatensor-core/.../CudaAadCodegen.java:485-510).
+ *   - java.lang.Math.max/min semantics (NaN-propagating, -0 < +0), which the
+ *     oracle uses (ScalarReplay.java:115-116).
+ *   - the deterministic warp -> block -> grid reduction of the accumulators
+ *     (atomic ticket, no spin-wait).
+ */
+#ifndef NT_DEVICE_RT_CUH
+#define NT_DEVICE_RT_CUH
+
+#ifdef NT_HOST
+#include <math.h>
+#include <string.h>
+#define NT_FN static inline
+#else
+#define NT_FN static __device__ __forceinline__
+#endif
+
+typedef unsigned int nt_u32;
+typedef unsigned long long nt_u64;
+
+#define NT_PHILOX_M 0xD256D193u
+#define NT_PHILOX_W 0x9E3779B9u
+#define NT_PHILOX_K0 0x1BD11BDAu
+#define NT_STREAM_MIX 0x9E3779B1u
+#define NT_UNIFORM_TAG 0x40000000u
+#define NT_UINT_SCALE 2.3283064365386963e-10
+#define NT_TWO_PI 6.283185307179586
+
+/* Per-(path, seed, stream) key words. */
+struct nt_key {
+  nt_u32 lo;
+  nt_u32 hi;
+};
+
+NT_FN nt_key nt_make_key(nt_u64 path, nt_u64 seed, int stream) {
+  nt_key k;
+  k.lo = (nt_u32)path ^ (nt_u32)seed;
+  k.hi = (nt_u32)(path >> 32) ^ (nt_u32)(seed >> 32);
+  if (stream != 0) k.hi ^= (nt_u32)stream * NT_STREAM_MIX;
+  return k;
+}
+
+NT_FN nt_u32 nt_mulhi(nt_u32 a, nt_u32 b) {
+#ifdef NT_HOST
+  return (nt_u32)(((nt_u64)a * (nt_u64)b) >> 32);
+#else
+  return __umulhi(a, b);
+#endif
+}
+
+/* Ten Philox2x32 rounds on counter (x0, x1).  The per-round keys are
+ * compile-time constants once the loop is unrolled. */
+NT_FN void nt_philox(nt_u32 x0, nt_u32 x1, nt_u32* o0, nt_u32* o1) {
+  nt_u32 key = NT_PHILOX_K0;
+#ifndef NT_HOST
+#pragma unroll
+#endif
+  for (int i = 0; i < 10; ++i) {
+    nt_u32 hi = nt_mulhi(NT_PHILOX_M, x0);
+    nt_u32 lo = NT_PHILOX_M * x0;
+    x0 = hi ^ key ^ x1;
+    x1 = lo;
+    key += NT_PHILOX_W;
+  }
+  *o0 = x0;
+  *o1 = x1;
+}
+
+/* Words of normal pair `pair` (draw ordinals 2*pair and 2*pair+1). */
+NT_FN void nt_normal_words(nt_key k, nt_u32 pair, nt_u32* w0, nt_u32* w1) {
+  nt_philox(k.lo, k.hi ^ pair, w0, w1);
+}
+
+/* fp64 Box-Muller of one block: cosine leg (even ordinal) and sine leg (odd). */
+NT_FN void nt_bm64(nt_u32 w0, nt_u32 w1, double* cos_leg, double* sin_leg) {
+  double u1 = ((double)w0 + 0.5) * NT_UINT_SCALE;
+  double u2 = ((double)w1 + 0.5) * NT_UINT_SCALE;
+  double r = sqrt(-2.0 * log(u1));
+  double a = NT_TWO_PI * u2;
+  double s, c;
+#ifdef NT_HOST
+  s = sin(a);
+  c = cos(a);
+#else
+  sincos(a, &s, &c);
+#endif
+  *cos_leg = r * c;
+  *sin_leg = r * s;
+}
+
+/* fp32 Box-Muller: the uint32 words are the fp64 generator's; u1 is rounded
+ * to the nearest float and clamped below 1 so the radius never collapses. */
+NT_FN void nt_bm32(nt_u32 w0, nt_u32 w1, float* cos_leg, float* sin_leg) {
+  const float scale = 2.3283064365386963e-10f; /* 2^-32, exact */
+  const float half_scale = 1.1641532182693481e-10f; /* 2^-33, exact */
+  const float below_one = 0.99999994039535522f; /* 1 - 2^-24 */
+  float u1 = fminf(fmaf((float)w0, scale, half_scale), below_one);
+  float u2 = fmaf((float)w1, scale, half_scale);
+  float r = sqrtf(-2.0f * logf(u1));
+  float a = 6.28318530717958648f * u2;
+  float s, c;
+#ifdef NT_HOST
+  s = sinf(a);
+  c = cosf(a);
+#else
+  sincosf(a, &s, &c);
+#endif
+  *cos_leg = r * c;
+  *sin_leg = r * s;
+}
+
+NT_FN void nt_normal_pair64(nt_key k, nt_u32 pair, double* c, double* s) {
+  nt_u32 w0, w1;
+  nt_normal_words(k, pair, &w0, &w1);
+  nt_bm64(w0, w1, c, s);
+}
+
+NT_FN void nt_normal_pair32(nt_key k, nt_u32 pair, float* c, float* s) {
+  nt_u32 w0, w1;
+  nt_normal_words(k, pair, &w0, &w1);
+  nt_bm32(w0, w1, c, s);
+}
+
+/* A single draw when its partner leg is not used in the same region. */
+NT_FN double nt_normal64(nt_key k, nt_u32 ordinal) {
+  double c, s;
+  nt_normal_pair64(k, ordinal >> 1, &c, &s);
+  return (ordinal & 1u) ? s : c;
+}
+
+NT_FN float nt_normal32(nt_key k, nt_u32 ordinal) {
+  float c, s;
+  nt_normal_pair32(k, ordinal >> 1, &c, &s);
+  return (ordinal & 1u) ? s : c;
+}
+
+NT_FN double nt_uniform64(nt_key k, nt_u32 ordinal) {
+  nt_u32 w0, w1;
+  nt_philox(k.lo, k.hi ^ (ordinal | NT_UNIFORM_TAG), &w0, &w1);
+  return ((double)w0 + 0.5) * NT_UINT_SCALE;
+}
+
+NT_FN float nt_uniform32(nt_key k, nt_u32 ordinal) {
+  return (float)nt_uniform64(k, ordinal);
+}
+
+/* A double from its IEEE-754 bits (non-finite tape constants). */
+NT_FN double nt_from_bits64(nt_u64 bits) {
+#ifdef NT_HOST
+  double x;
+  memcpy(&x, &bits, sizeof x);
+  return x;
+#else
+  return __longlong_as_double((long long)bits);
+#endif
+}
+
+/* ---- java.lang.Math semantics ------------------------------------------- */
+
+NT_FN bool nt_signbit64(double x) {
+#ifdef NT_HOST
+  long long bits;
+  memcpy(&bits, &x, sizeof bits);
+  return bits < 0;
+#else
+  return __double_as_longlong(x) < 0;
+#endif
+}
+
+NT_FN bool nt_signbit32(float x) {
+#ifdef NT_HOST
+  int bits;
+  memcpy(&bits, &x, sizeof bits);
+  return bits < 0;
+#else
+  return __float_as_int(x) < 0;
+#endif
+}
+
+NT_FN double nt_max64(double a, double b) {
+  if (a != a) return a;
+  if (a == 0.0 && b == 0.0 && nt_signbit64(a)) return b;
+  return a >= b ? a : b;
+}
+
+NT_FN double nt_min64(double a, double b) {
+  if (a != a) return a;
+  if (a == 0.0 && b == 0.0 && nt_signbit64(b)) return b;
+  return a <= b ? a : b;
+}
+
+NT_FN float nt_max32(float a, float b) {
+  if (a != a) return a;
+  if (a == 0.0f && b == 0.0f && nt_signbit32(a)) return b;
+  return a >= b ? a : b;
+}
+
+NT_FN float nt_min32(float a, float b) {
+  if (a != a) return a;
+  if (a == 0.0f && b == 0.0f && nt_signbit32(b)) return b;
+  return a <= b ? a : b;
+}
+
+/* Knuth's TwoSum: after the call s + c holds the exact value of the old
+ * s + c + x to within the rounding of c.  Per-thread accumulators use it so a
+ * thread's running sum over thousands of scenarios keeps full precision. */
+NT_FN void nt_two_sum(double* s, double* c, double x) {
+  const double t = *s + x;
+  const double bp = t - *s;
+  *c += (*s - (t - bp)) + (x - bp);
+  *s = t;
+}
+
+/* ---- deterministic reduction (device only) ------------------------------ */
+#ifndef NT_HOST
+
+NT_FN double nt_warp_sum(double x) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) x += __shfl_down_sync(0xffffffffu, x, off);
+  return x;
+}
+
+/*
+ * Reduces `channels` per-thread accumulators to one record per block, then the
+ * last block to finish (atomic ticket, no waiting) sums the block records in
+ * block order and writes (or adds) the grid total.  `scratch` must hold
+ * channels * (blockDim.x / 32) doubles of shared memory.
+ *   partials: gridDim.x * channels doubles (global)
+ *   ticket:   one counter, zero on entry, left zero on exit
+ *   out:      channels doubles; written when accumulate == 0, else added to
+ */
+NT_FN void nt_grid_reduce(const double* acc, int channels, double* scratch, double* partials,
+                          unsigned int* ticket, double* out, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  for (int c = 0; c < channels; ++c) {
+    double v = nt_warp_sum(acc[c]);
+    if (lane == 0) scratch[c * warps + warp] = v;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+    double s = 0.0;
+    for (int w = 0; w < warps; ++w) s += scratch[c * warps + w];
+    partials[(nt_u64)blockIdx.x * channels + c] = s;
+  }
+  __shared__ unsigned int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+      double s = 0.0;
+      for (unsigned int b = 0; b < gridDim.x; ++b) s += __ldcg(&partials[(nt_u64)b * channels + c]);
+      out[c] = accumulate ? out[c] + s : s;
+    }
+    if (threadIdx.x == 0) *ticket = 0u;
+  }
+}
+
+#endif /* !NT_HOST */
+
+#endif /* NT_DEVICE_RT_CUH */

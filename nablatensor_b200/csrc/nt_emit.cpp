@@ -1,0 +1,517 @@
+// nt_emit.cpp -- tape -> sm_100a CUDA C (or host C++) for one scenario per thread.
+//
+// Layout of the emitted scenario (one thread, one path at a time):
+//   prologue forward   straight-line, values in registers (v<i>)
+//   loop forward       rolled over units; every G units the checkpointed
+//                      carries go to shared memory (or global scratch)
+//   epilogue forward   straight-line; reads the last unit through cv/xv
+//   value accumulators
+//   per output:
+//     epilogue reverse straight-line adjoints d<i>; loop exits cd<k>/xd<j>
+//     loop reverse     per segment, last first: restore carries, recompute the
+//                      segment's G units into registers (r<g>_<j>), walk the
+//                      units backwards; invariant adjoints stay in registers
+//     prologue reverse
+//     adjoint accumulators
+// The adjoint rules and their order follow ScalarReplay.run's reverse switch
+// (nablatensor-engine-cpu/.../cpu/ScalarReplay.java:129-171), emitted only for
+// contributions into active arguments as the reference device sweep does
+// (nablatensor-core/.../CudaAadCodegen.java:386-448).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <sstream>
+
+#include "nt_internal.hpp"
+
+namespace nt {
+
+namespace {
+
+int nargs(int op) { return is_binary(op) ? 2 : (is_unary(op) ? 1 : 0); }
+
+struct Out {
+  std::string s;
+  int ind = 0;
+  void line(const std::string& x) {
+    s.append((size_t)ind * 2, ' ');
+    s += x;
+    s += '\n';
+  }
+  void open(const std::string& x) { line(x); ++ind; }
+  void close(const std::string& x = "}") { --ind; line(x); }
+};
+
+std::string lit(double x, bool f32) {
+  char buf[64];
+  if (std::isfinite(x)) {
+    std::snprintf(buf, sizeof buf, "%a", x);
+    std::string s(buf);
+    if (x < 0) s = "(" + s + ")";
+    return f32 ? "((float)" + s + ")" : s;
+  }
+  uint64_t bits;
+  std::memcpy(&bits, &x, sizeof bits);
+  std::snprintf(buf, sizeof buf, "nt_from_bits64(0x%016llxULL)", (unsigned long long)bits);
+  return f32 ? "((float)" + std::string(buf) + ")" : std::string(buf);
+}
+
+class Emitter {
+ public:
+  Emitter(const Tape& t, const Plan& p, const EmitConfig& cfg) : t_(t), p_(p), lp_(p.loop), cfg_(cfg) {}
+
+  std::string run();
+
+ private:
+  const Tape& t_;
+  const Plan& p_;
+  const Loop& lp_;
+  const EmitConfig& cfg_;
+  Out o_;
+
+  std::string R(const char* f64, const char* f32) const { return cfg_.f32 ? f32 : f64; }
+  int32_t channels() const { return t_.n_out() * (2 + t_.n_in()); }
+  bool in_loop(int32_t x) const { return lp_.in(x); }
+
+  // ---- names of outside nodes and loop exits ----
+  std::string val_outside(int32_t x) const {
+    if (in_loop(x)) {
+      const int32_t j = lp_.off(x);
+      return lp_.is_carry[j] ? "cv" + std::to_string(j) : "xv" + std::to_string(j);
+    }
+    return "v" + std::to_string(x);
+  }
+  std::string adj_outside(int32_t x) const {
+    if (in_loop(x)) {
+      const int32_t j = lp_.off(x);
+      return lp_.is_carry[j] ? "cd" + std::to_string(j) : "xd" + std::to_string(j);
+    }
+    return "d" + std::to_string(x);
+  }
+  bool active_outside(int32_t x) const { return in_loop(x) ? lp_.body[lp_.off(x)].active : t_.active[x] != 0; }
+
+  std::string fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a) const;
+  void emit_straight_forward(int32_t lo, int32_t hi);
+  void emit_straight_reverse(int32_t lo, int32_t hi);
+  void emit_rule(int op, const std::string& D, const std::string& Va, const std::string& Vb,
+                 const std::string& Vi, const std::string* da, const std::string* db);
+  void emit_body_forward(const std::string& pre, const std::string& unit, bool recompute, int g);
+  void emit_body_reverse(int g);
+  void emit_scenario();
+  void emit_reverse_for_output(int o);
+  void acc_line(int32_t k, const std::string& x);
+};
+
+std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a) const {
+  switch (op) {
+    case NT_CONST: return lit(c, cfg_.f32);
+    case NT_INPUT: return "in" + std::to_string(a);
+    case NT_ADD: return A + " + " + B;
+    case NT_SUB: return A + " - " + B;
+    case NT_MUL: return A + " * " + B;
+    case NT_DIV: return A + " / " + B;
+    case NT_NEG: return "-" + A;
+    case NT_EXP: return R("exp(", "expf(") + A + ")";
+    case NT_LOG: return R("log(", "logf(") + A + ")";
+    case NT_SQRT: return R("sqrt(", "sqrtf(") + A + ")";
+    case NT_ABS: return R("fabs(", "fabsf(") + A + ")";
+    case NT_MAX: return R("nt_max64(", "nt_max32(") + A + ", " + B + ")";
+    case NT_MIN: return R("nt_min64(", "nt_min32(") + A + ", " + B + ")";
+  }
+  fail(NT_E_INTERNAL, "fwd_expr: unexpected op");
+}
+
+// Adjoint contribution of one node (ScalarReplay.java:139-165).  da/db are
+// null when that argument is inactive (no contribution emitted).
+void Emitter::emit_rule(int op, const std::string& D, const std::string& Va, const std::string& Vb,
+                        const std::string& Vi, const std::string* da, const std::string* db) {
+  const std::string half = cfg_.f32 ? "0.5f" : "0.5";
+  const std::string zero = cfg_.f32 ? "0.0f" : "0.0";
+  switch (op) {
+    case NT_ADD:
+      if (da) o_.line(*da + " += " + D + ";");
+      if (db) o_.line(*db + " += " + D + ";");
+      break;
+    case NT_SUB:
+      if (da) o_.line(*da + " += " + D + ";");
+      if (db) o_.line(*db + " -= " + D + ";");
+      break;
+    case NT_MUL:
+      if (da) o_.line(*da + " += " + D + " * " + Vb + ";");
+      if (db) o_.line(*db + " += " + D + " * " + Va + ";");
+      break;
+    case NT_DIV:
+      if (da) o_.line(*da + " += " + D + " / " + Vb + ";");
+      if (db) o_.line(*db + " -= " + D + " * " + Vi + " / " + Vb + ";");
+      break;
+    case NT_NEG:
+      if (da) o_.line(*da + " -= " + D + ";");
+      break;
+    case NT_EXP:
+      if (da) o_.line(*da + " += " + D + " * " + Vi + ";");
+      break;
+    case NT_LOG:
+      if (da) o_.line(*da + " += " + D + " / " + Va + ";");
+      break;
+    case NT_SQRT:
+      if (da) o_.line(*da + " += " + D + " * " + half + " / " + Vi + ";");
+      break;
+    case NT_ABS:
+      if (da) o_.line(*da + " += " + Va + " < " + zero + " ? -" + D + " : " + D + ";");
+      break;
+    case NT_MAX:
+    case NT_MIN: {
+      const std::string cmp = "(" + Va + (op == NT_MAX ? " >= " : " <= ") + Vb + ")";
+      if (da && db) o_.line("if " + cmp + " " + *da + " += " + D + "; else " + *db + " += " + D + ";");
+      else if (da) o_.line("if " + cmp + " " + *da + " += " + D + ";");
+      else if (db) o_.line("if (!" + cmp + ") " + *db + " += " + D + ";");
+      break;
+    }
+    default: break;
+  }
+}
+
+// Straight-line forward over [lo, hi) (prologue or epilogue).  Normal draws
+// whose pair partner is in the same range share one Philox block.
+void Emitter::emit_straight_forward(int32_t lo, int32_t hi) {
+  std::map<std::pair<int32_t, int32_t>, std::vector<int32_t>> pairs;  // (stream, pair) -> nodes
+  for (int32_t i = lo; i < hi; ++i)
+    if (t_.op[i] == NT_RANDN) pairs[{t_.b[i], t_.a[i] >> 1}].push_back(i);
+  std::map<int32_t, bool> done;
+  const std::string real_t = "real";
+  for (int32_t i = lo; i < hi; ++i) {
+    const int op = t_.op[i];
+    const std::string vi = "v" + std::to_string(i);
+    if (op == NT_RANDN) {
+      if (done.count(i)) continue;
+      const auto& grp = pairs[{t_.b[i], t_.a[i] >> 1}];
+      int32_t even = -1, odd = -1;
+      for (int32_t x : grp) ((t_.a[x] & 1) ? odd : even) = x;
+      const std::string key = "key" + std::to_string(t_.b[i]);
+      if (even >= 0 && odd >= 0) {
+        o_.line("real v" + std::to_string(even) + ", v" + std::to_string(odd) + ";");
+        o_.line(R("nt_normal_pair64(", "nt_normal_pair32(") + key + ", " + std::to_string(t_.a[i] >> 1) +
+                "u, &v" + std::to_string(even) + ", &v" + std::to_string(odd) + ");");
+        done[even] = done[odd] = true;
+      } else {
+        o_.line("const real " + vi + " = " + R("nt_normal64(", "nt_normal32(") + key + ", " +
+                std::to_string(t_.a[i]) + "u);");
+      }
+      continue;
+    }
+    if (op == NT_RANDU) {
+      o_.line("const real " + vi + " = " + R("nt_uniform64(", "nt_uniform32(") + "key" +
+              std::to_string(t_.b[i]) + ", " + std::to_string(t_.a[i]) + "u);");
+      continue;
+    }
+    const std::string A = nargs(op) >= 1 ? val_outside(t_.a[i]) : "";
+    const std::string B = nargs(op) >= 2 ? val_outside(t_.b[i]) : "";
+    o_.line("const " + real_t + " " + vi + " = " + fwd_expr(op, A, B, t_.c[i], t_.a[i]) + ";");
+  }
+}
+
+void Emitter::emit_straight_reverse(int32_t lo, int32_t hi) {
+  for (int32_t i = hi - 1; i >= lo; --i) {
+    if (!t_.active[i]) continue;
+    const int op = t_.op[i];
+    if (nargs(op) == 0) continue;
+    const std::string D = "d" + std::to_string(i);
+    const int32_t a = t_.a[i], b = nargs(op) == 2 ? t_.b[i] : -1;
+    const std::string Va = val_outside(a), Vb = b >= 0 ? val_outside(b) : "", Vi = "v" + std::to_string(i);
+    std::string da = adj_outside(a), db = b >= 0 ? adj_outside(b) : "";
+    const bool aa = active_outside(a), ab = b >= 0 && active_outside(b);
+    emit_rule(op, D, Va, Vb, Vi, aa ? &da : nullptr, ab ? &db : nullptr);
+  }
+}
+
+// One unit of the loop body.  Forward loop: pre = "f", unit = "u".
+// Recompute: pre = "r<g>_", unit = "(s * G + g)", carry refs of unit 0 read the
+// restored segment-start carries cs<k>, later units read unit g-1.
+void Emitter::emit_body_forward(const std::string& pre, const std::string& unit, bool recompute, int g) {
+  const int32_t L = lp_.L;
+  auto name = [&](int32_t j) { return pre + std::to_string(j); };
+  auto ref = [&](const Ref& r) -> std::string {
+    if (r.kind == REF_SAME) return name(r.idx);
+    if (r.kind == REF_CARRY) {
+      if (!recompute) return "cv" + std::to_string(r.idx);
+      if (g == 0) return "cs" + std::to_string(r.idx);
+      return "r" + std::to_string(g - 1) + "_" + std::to_string(r.idx);
+    }
+    return val_outside(r.idx);
+  };
+  // Pairing of normal draws inside the unit.
+  std::map<int32_t, int32_t> partner;  // j -> partner j'
+  for (int32_t j = 0; j < L; ++j) {
+    const BodyNode& x = lp_.body[j];
+    if (x.op != NT_RANDN || (x.draw_stride & 1)) continue;
+    for (int32_t k = 0; k < L; ++k) {
+      const BodyNode& y = lp_.body[k];
+      if (k != j && y.op == NT_RANDN && y.stream == x.stream && y.draw_stride == x.draw_stride &&
+          (y.draw_base ^ 1) == x.draw_base) {
+        partner[j] = k;
+      }
+    }
+  }
+  std::vector<uint8_t> emitted(L, 0);
+  for (int32_t j = 0; j < L; ++j) {
+    if (recompute && !lp_.recompute[j]) continue;
+    if (emitted[j]) continue;
+    const BodyNode& bn = lp_.body[j];
+    const std::string key = "key" + std::to_string(bn.stream);
+    if (bn.op == NT_RANDN) {
+      auto it = partner.find(j);
+      if (it != partner.end()) {
+        const int32_t k = it->second;
+        const int32_t ev = (bn.draw_base & 1) ? k : j, od = (bn.draw_base & 1) ? j : k;
+        const int32_t pb = lp_.body[ev].draw_base >> 1, ps = bn.draw_stride >> 1;
+        o_.line(R("nt_normal_pair64(", "nt_normal_pair32(") + key + ", (nt_u32)(" + std::to_string(pb) + " + " +
+                unit + " * " + std::to_string(ps) + "), &" + name(ev) + ", &" + name(od) + ");");
+        emitted[ev] = emitted[od] = 1;
+      } else {
+        o_.line(name(j) + " = " + R("nt_normal64(", "nt_normal32(") + key + ", (nt_u32)(" +
+                std::to_string(bn.draw_base) + " + " + unit + " * " + std::to_string(bn.draw_stride) + "));");
+        emitted[j] = 1;
+      }
+      continue;
+    }
+    if (bn.op == NT_RANDU) {
+      o_.line(name(j) + " = " + R("nt_uniform64(", "nt_uniform32(") + key + ", (nt_u32)(" +
+              std::to_string(bn.draw_base) + " + " + unit + " * " + std::to_string(bn.draw_stride) + "));");
+      emitted[j] = 1;
+      continue;
+    }
+    const std::string A = nargs(bn.op) >= 1 ? ref(bn.ra) : "";
+    const std::string B = nargs(bn.op) >= 2 ? ref(bn.rb) : "";
+    o_.line(name(j) + " = " + fwd_expr(bn.op, A, B, bn.c, -1) + ";");
+    emitted[j] = 1;
+  }
+}
+
+// Reverse of unit g of the current segment (values from the recompute).
+void Emitter::emit_body_reverse(int g) {
+  const int32_t L = lp_.L;
+  const std::string G = std::to_string(g);
+  auto val = [&](const Ref& r) -> std::string {
+    if (r.kind == REF_SAME) return "r" + G + "_" + std::to_string(r.idx);
+    if (r.kind == REF_CARRY) {
+      if (g == 0) return "cs" + std::to_string(r.idx);
+      return "r" + std::to_string(g - 1) + "_" + std::to_string(r.idx);
+    }
+    return val_outside(r.idx);
+  };
+  auto adj = [&](const Ref& r, bool* active) -> std::string {
+    if (r.kind == REF_SAME) { *active = lp_.body[r.idx].active; return "b" + std::to_string(r.idx); }
+    if (r.kind == REF_CARRY) { *active = lp_.body[r.idx].active; return "n" + std::to_string(r.idx); }
+    *active = t_.active[r.idx] != 0;
+    return "d" + std::to_string(r.idx);
+  };
+  o_.open("{");
+  for (int32_t j = 0; j < L; ++j) {
+    const BodyNode& bn = lp_.body[j];
+    if (!bn.active) continue;
+    std::string init = cfg_.f32 ? "0.0f" : "0.0";
+    if (lp_.is_carry[j]) init = "cd" + std::to_string(j);
+    else if (lp_.is_exit[j]) init = "xd" + std::to_string(j);
+    o_.line("real b" + std::to_string(j) + " = " + init + ";");
+  }
+  for (int32_t k : lp_.carries)
+    if (lp_.body[k].active) o_.line("real n" + std::to_string(k) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+  for (int32_t j = L - 1; j >= 0; --j) {
+    const BodyNode& bn = lp_.body[j];
+    if (!bn.active || nargs(bn.op) == 0) continue;
+    bool aa = false, ab = false;
+    std::string da = adj(bn.ra, &aa);
+    std::string db = nargs(bn.op) == 2 ? adj(bn.rb, &ab) : "";
+    const std::string Va = val(bn.ra), Vb = nargs(bn.op) == 2 ? val(bn.rb) : "";
+    const std::string Vi = "r" + G + "_" + std::to_string(j);
+    emit_rule(bn.op, "b" + std::to_string(j), Va, Vb, Vi, aa ? &da : nullptr, ab ? &db : nullptr);
+  }
+  for (int32_t k : lp_.carries)
+    if (lp_.body[k].active) o_.line("cd" + std::to_string(k) + " = n" + std::to_string(k) + ";");
+  for (int32_t j : lp_.exits)
+    if (!lp_.is_carry[j] && lp_.body[j].active) o_.line("xd" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+  o_.close();
+}
+
+void Emitter::emit_reverse_for_output(int o) {
+  const std::string zero = cfg_.f32 ? "0.0f" : "0.0";
+  const std::string one = cfg_.f32 ? "1.0f" : "1.0";
+  const int32_t out = t_.output_node[o];
+  const int32_t stride = 2 + t_.n_in();
+  o_.open("{  // reverse sweep, output " + std::to_string(o));
+  // Adjoint registers of every active node outside the loop.
+  for (int32_t i = 0; i < t_.n; ++i) {
+    if (in_loop(i) || !t_.active[i]) continue;
+    o_.line("real d" + std::to_string(i) + " = " + zero + ";");
+  }
+  if (lp_.present) {
+    for (int32_t k : lp_.carries)
+      if (lp_.body[k].active) o_.line("real cd" + std::to_string(k) + " = " + zero + ";");
+    for (int32_t j : lp_.exits)
+      if (!lp_.is_carry[j] && lp_.body[j].active) o_.line("real xd" + std::to_string(j) + " = " + zero + ";");
+  }
+  if (active_outside(out)) o_.line(adj_outside(out) + " = " + one + ";");
+
+  if (!lp_.present) {
+    emit_straight_reverse(0, t_.n);
+  } else {
+    emit_straight_reverse(lp_.end(), t_.n);
+    const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
+    const int32_t nck = (int32_t)lp_.ckpt.size();
+    o_.open("for (int s = " + std::to_string(K - 1) + "; s >= 0; --s) {");
+    for (int32_t c = 0; c < nck; ++c)
+      o_.line("const real cs" + std::to_string(lp_.ckpt[c]) + " = NT_CK(s * " + std::to_string(nck) + " + " +
+              std::to_string(c) + ");");
+    for (int g = 0; g < G; ++g) {
+      std::string decl;
+      for (int32_t j = 0; j < L; ++j)
+        decl += (decl.empty() ? "real " : ", ") + ("r" + std::to_string(g) + "_" + std::to_string(j));
+      o_.line(decl + ";");
+    }
+    for (int g = 0; g < G; ++g) {
+      o_.line("// recompute unit " + std::to_string(g));
+      emit_body_forward("r" + std::to_string(g) + "_", "(s * " + std::to_string(G) + " + " + std::to_string(g) + ")",
+                        true, g);
+    }
+    for (int g = G - 1; g >= 0; --g) emit_body_reverse(g);
+    o_.close();
+    // Unit 0's carry adjoints belong to the carries' initial values.
+    for (size_t c = 0; c < lp_.carries.size(); ++c) {
+      const int32_t k = lp_.carries[c], x = lp_.carry_init[c];
+      if (lp_.body[k].active && t_.active[x]) o_.line("d" + std::to_string(x) + " += cd" + std::to_string(k) + ";");
+    }
+    emit_straight_reverse(0, lp_.B);
+  }
+  for (int32_t j = 0; j < t_.n_in(); ++j) {
+    const int32_t node = t_.input_node[j];
+    acc_line(o * stride + 2 + j, "(double)" + adj_outside(node));
+  }
+  o_.close();
+}
+
+// Per-thread accumulation: compensated (TwoSum) on the device; a plain
+// running sum in the host target, which reproduces AadTotals.add exactly.
+void Emitter::acc_line(int32_t k, const std::string& x) {
+  const std::string K = std::to_string(k);
+  if (cfg_.target == 1) o_.line("nt_acc[" + K + "] += " + x + ";");
+  else o_.line("nt_two_sum(&nt_acc[" + K + "], &nt_cmp[" + K + "], " + x + ");");
+}
+
+void Emitter::emit_scenario() {
+  // Stream keys.
+  std::vector<uint8_t> used(t_.n_streams, 0);
+  for (int32_t i = 0; i < t_.n; ++i)
+    if (is_draw(t_.op[i])) used[t_.b[i]] = 1;
+  for (int32_t s = 0; s < t_.n_streams; ++s)
+    if (used[s]) o_.line("const nt_key key" + std::to_string(s) + " = nt_make_key(path, seed, " + std::to_string(s) + ");");
+
+  if (!lp_.present) {
+    emit_straight_forward(0, t_.n);
+  } else {
+    const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
+    emit_straight_forward(0, lp_.B);
+    o_.line("// step loop: " + std::to_string(lp_.N) + " units of " + std::to_string(L) + " nodes (" +
+            std::to_string(lp_.steps_per_unit) + " steps each), " + std::to_string(K) + " segments of " +
+            std::to_string(G) + " units");
+    for (size_t c = 0; c < lp_.carries.size(); ++c)
+      o_.line("real cv" + std::to_string(lp_.carries[c]) + " = " + val_outside(lp_.carry_init[c]) + ";");
+    for (int32_t j : lp_.exits)
+      if (!lp_.is_carry[j]) o_.line("real xv" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+    const int32_t nck = (int32_t)lp_.ckpt.size();
+    o_.open("for (int s = 0; s < " + std::to_string(K) + "; ++s) {");
+    for (int32_t c = 0; c < nck; ++c)
+      o_.line("NT_CK(s * " + std::to_string(nck) + " + " + std::to_string(c) + ") = cv" + std::to_string(lp_.ckpt[c]) + ";");
+    if (cfg_.target == 0) o_.line("#pragma unroll 1");
+    o_.open("for (int g = 0; g < " + std::to_string(G) + "; ++g) {");
+    o_.line("const int u = s * " + std::to_string(G) + " + g;");
+    std::string decl;
+    for (int32_t j = 0; j < L; ++j) decl += (j ? ", f" : "real f") + std::to_string(j);
+    o_.line(decl + ";");
+    emit_body_forward("f", "u", false, 0);
+    for (int32_t k : lp_.carries) o_.line("cv" + std::to_string(k) + " = f" + std::to_string(k) + ";");
+    for (int32_t j : lp_.exits)
+      if (!lp_.is_carry[j]) o_.line("xv" + std::to_string(j) + " = f" + std::to_string(j) + ";");
+    o_.close();
+    o_.close();
+    emit_straight_forward(lp_.end(), t_.n);
+  }
+  const int32_t stride = 2 + t_.n_in();
+  for (int32_t o = 0; o < t_.n_out(); ++o) {
+    const std::string y = "(double)" + val_outside(t_.output_node[o]);
+    acc_line(o * stride, y);
+    acc_line(o * stride + 1, y + " * " + y);
+  }
+  if (cfg_.adjoints)
+    for (int32_t o = 0; o < t_.n_out(); ++o) emit_reverse_for_output(o);
+}
+
+std::string Emitter::run() {
+  const bool host = cfg_.target == 1;
+  const int32_t nck_total = ckpt_values(p_);
+  o_.line("// Generated by libnabla_b200 from a " + std::to_string(t_.n) + "-node tape.");
+  if (host) {
+    o_.line("#define NT_HOST 1");
+    o_.line("#include <stdint.h>");
+  }
+  o_.line("#include \"nt_device_rt.cuh\"");
+  o_.line(std::string("typedef ") + (cfg_.f32 ? "float" : "double") + " real;");
+  o_.line("#define NT_CH " + std::to_string(channels()));
+  if (host) {
+    o_.line("#define NT_CK(slot) nt_ckbuf[(slot)]");
+    o_.open("extern \"C\" void nt_host_replay(const double* inputs, uint64_t n_paths, uint64_t path_offset, uint64_t seed, double* sums) {");
+    for (int32_t j = 0; j < t_.n_in(); ++j)
+      o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
+    o_.line("double nt_acc[NT_CH];");
+    o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = 0.0;");
+    o_.line("real nt_ckbuf[" + std::to_string(std::max(1, nck_total)) + "];");
+    o_.line("(void)nt_ckbuf;");
+    o_.open("for (nt_u64 p = 0; p < n_paths; ++p) {");
+    o_.line("const nt_u64 path = p + path_offset;");
+    emit_scenario();
+    o_.close();
+    o_.line("for (int c = 0; c < NT_CH; ++c) sums[c] = nt_acc[c];");
+    o_.close();
+    return o_.s;
+  }
+  o_.line("#define NT_BLOCK " + std::to_string(cfg_.block));
+  if (cfg_.global_ckpt) {
+    o_.line("#define NT_CK(slot) nt_gck[(nt_u64)(slot) * nt_gthreads + nt_gtid]");
+  } else {
+    o_.line("#define NT_CK(slot) nt_ck[(slot) * NT_BLOCK + threadIdx.x]");
+  }
+  std::string bounds = "__launch_bounds__(NT_BLOCK" + (cfg_.min_blocks > 0 ? ", " + std::to_string(cfg_.min_blocks) : std::string()) + ")";
+  o_.line("extern \"C\" __global__ void " + bounds + " nt_replay_kernel(");
+  o_.line("    const double* __restrict__ inputs, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
+  o_.line("    double* __restrict__ partials, unsigned int* __restrict__ ticket, double* __restrict__ out,");
+  o_.line("    int accumulate, real* __restrict__ nt_gck) {");
+  ++o_.ind;
+  if (!cfg_.global_ckpt) o_.line("extern __shared__ real nt_ck[];");
+  o_.line("__shared__ double nt_red[NT_CH * (NT_BLOCK / 32)];");
+  o_.line("const nt_u64 nt_gtid = (nt_u64)blockIdx.x * NT_BLOCK + threadIdx.x;");
+  o_.line("const nt_u64 nt_gthreads = (nt_u64)gridDim.x * NT_BLOCK;");
+  o_.line("(void)nt_gck; (void)nt_gthreads;");
+  for (int32_t j = 0; j < t_.n_in(); ++j)
+    o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
+  o_.line("double nt_acc[NT_CH], nt_cmp[NT_CH];");
+  o_.line("#pragma unroll");
+  o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
+  o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
+  o_.line("const nt_u64 path = p + path_offset;");
+  emit_scenario();
+  o_.close();
+  o_.line("#pragma unroll");
+  o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] += nt_cmp[c];");
+  o_.line("nt_grid_reduce(nt_acc, NT_CH, nt_red, partials, ticket, out, accumulate);");
+  o_.close();
+  return o_.s;
+}
+
+}  // namespace
+
+std::string emit(const Tape& t, const Plan& p, const EmitConfig& cfg) {
+  Emitter e(t, p, cfg);
+  return e.run();
+}
+
+}  // namespace nt

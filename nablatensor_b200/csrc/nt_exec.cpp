@@ -1,0 +1,435 @@
+// nt_exec.cpp -- executables: device state, launch, reduction read-back,
+// scenario-range sharding with one NCCL all-reduce.
+//
+// The reference's device executable (nablatensor-core/.../DeviceAadExecutable.java:140-221)
+// launched 256-thread blocks over min(ceil(paths/256), 4096) blocks, copied
+// one partial record per block to the host and summed there.  Here:
+//   - one persistent grid of (SMs x resident blocks) walks the path range;
+//   - the grid reduction finishes on the device (atomic ticket, no spin) and
+//     the host reads n_out*(2+n_in) doubles;
+//   - long runs accumulate on the device across dispatches;
+//   - several GPUs split the range into contiguous shards and all-reduce the
+//     sums vector once (NCCL over NVLink/NVSwitch).
+#include "nt_exec.hpp"
+
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <thread>
+
+namespace nt {
+
+// ---- driver API through the runtime's entry-point query (no libcuda link) ----
+
+namespace {
+
+struct Driver {
+  CUresult (*moduleLoadData)(CUmodule*, const void*) = nullptr;
+  CUresult (*moduleUnload)(CUmodule) = nullptr;
+  CUresult (*moduleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
+  CUresult (*launchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                           CUstream, void**, void**) = nullptr;
+  CUresult (*funcGetAttribute)(int*, CUfunction_attribute, CUfunction) = nullptr;
+  CUresult (*funcSetAttribute)(CUfunction, CUfunction_attribute, int) = nullptr;
+  CUresult (*occupancy)(int*, CUfunction, int, size_t) = nullptr;
+  CUresult (*getErrorName)(CUresult, const char**) = nullptr;
+  bool ok = false;
+};
+
+template <class F>
+void entry(const char* name, F& fn) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &p, 12000, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+    fail(NT_E_CUDA, std::string("driver entry point unavailable: ") + name);
+  fn = reinterpret_cast<F>(p);
+}
+
+Driver& driver() {
+  static Driver d;
+  static std::once_flag once;
+  static std::string err;
+  std::call_once(once, [] {
+    try {
+      entry("cuModuleLoadData", d.moduleLoadData);
+      entry("cuModuleUnload", d.moduleUnload);
+      entry("cuModuleGetFunction", d.moduleGetFunction);
+      entry("cuLaunchKernel", d.launchKernel);
+      entry("cuFuncGetAttribute", d.funcGetAttribute);
+      entry("cuFuncSetAttribute", d.funcSetAttribute);
+      entry("cuOccupancyMaxActiveBlocksPerMultiprocessor", d.occupancy);
+      entry("cuGetErrorName", d.getErrorName);
+      d.ok = true;
+    } catch (const Error& e) {
+      err = e.what();
+    }
+  });
+  if (!d.ok) fail(NT_E_CUDA, err.empty() ? "CUDA driver unavailable" : err);
+  return d;
+}
+
+void cu_check(CUresult r, const char* what) {
+  if (r == CUDA_SUCCESS) return;
+  const char* name = "?";
+  if (driver().getErrorName) driver().getErrorName(r, &name);
+  fail(NT_E_CUDA, std::string(what) + ": " + name);
+}
+
+// ---- NCCL through dlopen (the process may already hold torch's copy) ----
+
+struct Nccl {
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*commFinalize)(ncclComm_t) = nullptr;
+  ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  const char* (*getErrorString)(ncclResult_t) = nullptr;
+  bool ok = false;
+  std::string err;
+};
+
+Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      n.err = std::string("cannot load libnccl.so.2: ") + dlerror();
+      return;
+    }
+    auto sym = [&](const char* s) { return dlsym(h, s); };
+    n.getUniqueId = (decltype(n.getUniqueId))sym("ncclGetUniqueId");
+    n.commInitRankConfig = (decltype(n.commInitRankConfig))sym("ncclCommInitRankConfig");
+    n.commGetAsyncError = (decltype(n.commGetAsyncError))sym("ncclCommGetAsyncError");
+    n.commAbort = (decltype(n.commAbort))sym("ncclCommAbort");
+    n.commDestroy = (decltype(n.commDestroy))sym("ncclCommDestroy");
+    n.commFinalize = (decltype(n.commFinalize))sym("ncclCommFinalize");
+    n.allReduce = (decltype(n.allReduce))sym("ncclAllReduce");
+    n.getErrorString = (decltype(n.getErrorString))sym("ncclGetErrorString");
+    n.ok = n.getUniqueId && n.commInitRankConfig && n.commGetAsyncError && n.commAbort && n.commDestroy &&
+           n.allReduce && n.getErrorString;
+    if (!n.ok) n.err = "libnccl.so.2 lacks a required symbol";
+  });
+  if (!n.ok) fail(NT_E_NCCL, n.err);
+  return n;
+}
+
+void nccl_check(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess || r == ncclInProgress) return;
+  fail(NT_E_NCCL, std::string(what) + ": " + nccl().getErrorString(r));
+}
+
+// Polls a non-blocking communicator until its pending work is enqueued or the
+// deadline passes; on expiry the communicator is aborted.
+void nccl_wait(ncclComm_t comm, int timeout_ms, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    nccl().commGetAsyncError(comm, &st);
+    if (st == ncclSuccess) return;
+    if (st != ncclInProgress) {
+      nccl().commAbort(comm);
+      fail(NT_E_NCCL, std::string(what) + ": " + nccl().getErrorString(st));
+    }
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      nccl().commAbort(comm);
+      fail(NT_E_NCCL, std::string(what) + ": timed out");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+}  // namespace
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return;
+  const int code = e == cudaErrorMemoryAllocation ? NT_E_OOM : NT_E_CUDA;
+  fail(code, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+// ---- compile / set-up ---------------------------------------------------------
+
+Exec* Exec::create(const nt_tape* tape, const nt_options* opt) {
+  if (!opt) fail(NT_E_INVALID_ARG, "options are null");
+  if (opt->precision != NT_FLOAT32 && opt->precision != NT_FLOAT64) fail(NT_E_INVALID_ARG, "bad precision");
+  std::unique_ptr<Exec> x(new Exec());
+  x->tape = ingest(tape);
+  x->cfg.f32 = opt->precision == NT_FLOAT32;
+  x->cfg.adjoints = opt->adjoints != 0;
+  x->cfg.no_loop = (opt->flags & NT_FLAG_NO_LOOP) != 0;
+  x->cfg.global_ckpt = (opt->flags & NT_FLAG_GLOBAL_CKPT) != 0;
+  x->cfg.block = opt->block > 0 ? opt->block : 128;
+  if (x->cfg.block % 32 != 0 || x->cfg.block > 1024) fail(NT_E_INVALID_ARG, "block must be a multiple of 32, <= 1024");
+  x->cfg.min_blocks = opt->min_blocks;
+  x->cfg.seg_units = opt->seg_units;
+  x->cfg.target = 0;
+  x->device = opt->device;
+  x->use_disk_cache = (opt->flags & NT_FLAG_NO_DISK_CACHE) == 0;
+  x->plan = plan_tape(x->tape, x->cfg);
+  x->channels = x->tape.n_out() * (2 + x->tape.n_in());
+  const size_t real_bytes = x->cfg.f32 ? 4 : 8;
+  // Checkpoints in shared memory unless they would starve occupancy.
+  const size_t ck_bytes = (size_t)ckpt_values(x->plan) * x->cfg.block * real_bytes;
+  if (!x->cfg.global_ckpt && ck_bytes > 96 * 1024) x->cfg.global_ckpt = true;
+  x->dyn_smem = x->cfg.global_ckpt ? 0 : (int)ck_bytes;
+  x->source = emit(x->tape, x->plan, x->cfg);
+  x->inputs.assign(x->tape.n_in(), 0.0);
+  for (int32_t j = 0; j < x->tape.n_in(); ++j) x->inputs[j] = tape->constant[x->tape.input_node[j]];
+  x->load(opt->max_regs);
+  return x.release();
+}
+
+void Exec::bind() const { cuda_check(cudaSetDevice(device), "cudaSetDevice"); }
+
+void Exec::load(int max_regs) {
+  int ndev = 0;
+  cuda_check(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) fail(NT_E_INVALID_ARG, "device ordinal out of range");
+  bind();
+  cudaDeviceProp prop;
+  cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10) fail(NT_E_UNSUPPORTED, std::string("this engine targets sm_100 (B200); device is ") + prop.name);
+  sm_count = prop.multiProcessorCount;
+  (void)max_regs;
+  double secs = 0.0;
+  std::vector<char> cubin = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs);
+  const auto t0 = std::chrono::steady_clock::now();
+  Driver& d = driver();
+  cu_check(d.moduleLoadData(&module, cubin.data()), "cuModuleLoadData");
+  cu_check(d.moduleGetFunction(&function, module, "nt_replay_kernel"), "cuModuleGetFunction");
+  if (dyn_smem > 48 * 1024)
+    cu_check(d.funcSetAttribute(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_smem),
+             "cuFuncSetAttribute");
+  int regs = 0, local = 0, ssm = 0;
+  cu_check(d.funcGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, function), "cuFuncGetAttribute");
+  cu_check(d.funcGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, function), "cuFuncGetAttribute");
+  cu_check(d.funcGetAttribute(&ssm, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, function), "cuFuncGetAttribute");
+  int per_sm = 0;
+  cu_check(d.occupancy(&per_sm, function, cfg.block, (size_t)dyn_smem), "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+  if (per_sm < 1) fail(NT_E_CUDA, "kernel does not fit on an SM");
+  blocks_per_sm = per_sm;
+  grid = sm_count * per_sm;
+  cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaMalloc(&d_inputs, sizeof(double) * std::max<int32_t>(1, tape.n_in())), "cudaMalloc inputs");
+  cuda_check(cudaMalloc(&d_partials, sizeof(double) * (size_t)grid * channels), "cudaMalloc partials");
+  cuda_check(cudaMalloc(&d_ticket, sizeof(unsigned int)), "cudaMalloc ticket");
+  cuda_check(cudaMalloc(&d_out, sizeof(double) * channels), "cudaMalloc out");
+  cuda_check(cudaMalloc(&d_acc, sizeof(double) * channels), "cudaMalloc accumulator");
+  cuda_check(cudaMalloc(&d_red, sizeof(double) * channels), "cudaMalloc reduced");
+  cuda_check(cudaMemset(d_ticket, 0, sizeof(unsigned int)), "cudaMemset ticket");
+  cuda_check(cudaMemset(d_acc, 0, sizeof(double) * channels), "cudaMemset accumulator");
+  if (cfg.global_ckpt && ckpt_values(plan) > 0) {
+    const size_t bytes = (size_t)ckpt_values(plan) * grid * cfg.block * (cfg.f32 ? 4 : 8);
+    cuda_check(cudaMalloc(&d_gck, bytes), "cudaMalloc checkpoints");
+  }
+  cuda_check(cudaMallocHost(&h_stage, sizeof(double) * (tape.n_in() + 2 * channels + 2)), "cudaMallocHost");
+  compile_seconds = secs + std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  std::memset(&info, 0, sizeof info);
+  info.registers = regs;
+  info.local_bytes = local;
+  info.static_smem = ssm;
+  info.dynamic_smem = dyn_smem;
+  info.block = cfg.block;
+  info.blocks_per_sm = per_sm;
+  info.grid = grid;
+  info.sm_count = sm_count;
+  info.channels = channels;
+  const Loop& lp = plan.loop;
+  info.loop_start = lp.present ? lp.B : -1;
+  info.loop_unit = lp.present ? lp.L : 0;
+  info.loop_units = lp.present ? lp.N : 0;
+  info.steps_per_unit = lp.present ? lp.steps_per_unit : 0;
+  info.seg_units = lp.present ? lp.G : 0;
+  info.segments = lp.present ? lp.K : 0;
+  info.ckpt_slots = lp.present ? (int32_t)lp.ckpt.size() : 0;
+  info.stored_per_unit = plan.stored_per_unit;
+  info.ckpt_global = cfg.global_ckpt ? 1 : 0;
+  info.compile_seconds = compile_seconds;
+  info.fwd_flops = plan.fwd_flops;
+  info.rev_flops = plan.rev_flops;
+}
+
+Exec::~Exec() {
+  if (comm) {
+    nccl().commDestroy((ncclComm_t)comm);
+    comm = nullptr;
+  }
+  if (device >= 0) cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
+  cudaFree(d_inputs);
+  cudaFree(d_partials);
+  cudaFree(d_ticket);
+  cudaFree(d_out);
+  cudaFree(d_acc);
+  cudaFree(d_red);
+  cudaFree(d_gck);
+  if (h_stage) cudaFreeHost(h_stage);
+  if (stream) cudaStreamDestroy(stream);
+  if (module) driver().moduleUnload(module);
+}
+
+// ---- launch ---------------------------------------------------------------------
+
+void Exec::upload_inputs_if_dirty() {
+  if (!dirty) return;
+  std::memcpy(h_stage, inputs.data(), sizeof(double) * inputs.size());
+  if (!inputs.empty())
+    cuda_check(cudaMemcpyAsync(d_inputs, h_stage, sizeof(double) * inputs.size(), cudaMemcpyHostToDevice, stream),
+               "upload inputs");
+  dirty = false;
+}
+
+void Exec::launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, int accumulate) {
+  if (paths == 0) fail(NT_E_INVALID_ARG, "paths must be positive");
+  const uint64_t need = (paths + cfg.block - 1) / cfg.block;
+  const unsigned g = (unsigned)std::min<uint64_t>(need, (uint64_t)grid);
+  void* gck = d_gck;
+  unsigned long long n = paths, off = offset, sd = seed;
+  void* args[] = {&d_inputs, &n, &off, &sd, &d_partials, &d_ticket, &out, &accumulate, &gck};
+  cu_check(driver().launchKernel(function, g, 1, 1, (unsigned)cfg.block, 1, 1, (unsigned)dyn_smem,
+                                 (CUstream)stream, args, nullptr),
+           "cuLaunchKernel");
+  ++launches;
+}
+
+void Exec::replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, double* seconds) {
+  const auto t0 = std::chrono::steady_clock::now();
+  bind();
+  upload_inputs_if_dirty();
+  launch(paths, offset, seed, d_out, 0);
+  double* h_out = h_stage + tape.n_in();
+  cuda_check(cudaMemcpyAsync(h_out, d_out, sizeof(double) * channels, cudaMemcpyDeviceToHost, stream), "read sums");
+  cuda_check(cudaStreamSynchronize(stream), "replay");
+  std::memcpy(sums, h_out, sizeof(double) * channels);
+  if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+void Exec::accumulate(uint64_t paths, uint64_t offset, uint64_t seed) {
+  bind();
+  upload_inputs_if_dirty();
+  launch(paths, offset, seed, d_acc, 1);
+}
+
+void Exec::read_accumulator(double* sums, bool reset) {
+  bind();
+  double* h_out = h_stage + tape.n_in();
+  cuda_check(cudaMemcpyAsync(h_out, d_acc, sizeof(double) * channels, cudaMemcpyDeviceToHost, stream), "read sums");
+  if (reset) cuda_check(cudaMemsetAsync(d_acc, 0, sizeof(double) * channels, stream), "reset accumulator");
+  cuda_check(cudaStreamSynchronize(stream), "read accumulator");
+  std::memcpy(sums, h_out, sizeof(double) * channels);
+}
+
+// ---- sharding + all-reduce ------------------------------------------------------
+
+void shard_range(uint64_t total, uint64_t offset, int32_t nranks, int32_t rank, uint64_t* from, uint64_t* count) {
+  if (nranks < 1 || rank < 0 || rank >= nranks) fail(NT_E_INVALID_ARG, "bad rank / world size");
+  const uint64_t r = (uint64_t)rank, n = (uint64_t)nranks;
+  const uint64_t base = total / n, extra = total % n;
+  *from = offset + r * base + std::min(r, extra);
+  *count = base + (r < extra ? 1 : 0);
+}
+
+void Exec::shard(uint64_t total, uint64_t offset, uint64_t* from, uint64_t* count) const {
+  shard_range(total, offset, nranks, rank, from, count);
+}
+
+void Exec::sharded_enqueue(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk) {
+  if (total == 0) fail(NT_E_INVALID_ARG, "paths must be positive");
+  bind();
+  upload_inputs_if_dirty();
+  uint64_t from = 0, count = 0;
+  shard(total, offset, &from, &count);
+  cuda_check(cudaMemsetAsync(d_acc, 0, sizeof(double) * channels, stream), "reset accumulator");
+  const uint64_t step = chunk > 0 ? chunk : count;
+  for (uint64_t done = 0; done < count; done += step) {
+    const uint64_t k = std::min(step, count - done);
+    launch(k, from + done, seed, d_acc, 1);
+  }
+  if (nranks > 1) {
+    if (!comm) fail(NT_E_STATE, "executable is not attached to a communicator");
+    nccl_check(nccl().allReduce(d_acc, d_acc, (size_t)channels, ncclFloat64, ncclSum, (ncclComm_t)comm, stream),
+               "ncclAllReduce");
+    nccl_wait((ncclComm_t)comm, dist_timeout_ms, "ncclAllReduce");
+  }
+}
+
+void Exec::sharded(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk, double* sums, double* seconds) {
+  const auto t0 = std::chrono::steady_clock::now();
+  sharded_enqueue(total, offset, seed, chunk);
+  // Bounded wait: a peer that never joins the all-reduce ends this call with
+  // an error instead of a hang.
+  if (nranks > 1) {
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(dist_timeout_ms) +
+                          std::chrono::seconds(600);
+    for (;;) {
+      cudaError_t q = cudaStreamQuery(stream);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) cuda_check(q, "sharded replay");
+      ncclResult_t st = ncclSuccess;
+      nccl().commGetAsyncError((ncclComm_t)comm, &st);
+      if (st != ncclSuccess && st != ncclInProgress) {
+        nccl().commAbort((ncclComm_t)comm);
+        comm = nullptr;
+        fail(NT_E_NCCL, std::string("all-reduce failed: ") + nccl().getErrorString(st));
+      }
+      if (std::chrono::steady_clock::now() > deadline) {
+        nccl().commAbort((ncclComm_t)comm);
+        comm = nullptr;
+        fail(NT_E_NCCL, "all-reduce timed out");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+  }
+  read_accumulator(sums, true);
+  if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+void Exec::attach(int32_t n, int32_t r, const uint8_t id[128], int32_t timeout_ms) {
+  if (n < 1 || r < 0 || r >= n) fail(NT_E_INVALID_ARG, "bad rank / world size");
+  if (comm) fail(NT_E_STATE, "already attached");
+  nranks = n;
+  rank = r;
+  dist_timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+  if (n == 1) return;
+  bind();
+  ncclUniqueId uid;
+  static_assert(sizeof(uid.internal) == 128, "NCCL unique id is 128 bytes");
+  std::memcpy(uid.internal, id, 128);
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  ncclComm_t c = nullptr;
+  nccl_check(nccl().commInitRankConfig(&c, n, uid, r, &config), "ncclCommInitRankConfig");
+  comm = c;
+  try {
+    nccl_wait(c, dist_timeout_ms, "ncclCommInitRank");
+  } catch (...) {
+    comm = nullptr;
+    throw;
+  }
+}
+
+void Exec::detach() {
+  if (comm) {
+    bind();
+    cudaStreamSynchronize(stream);
+    nccl().commDestroy((ncclComm_t)comm);
+    comm = nullptr;
+  }
+  nranks = 1;
+  rank = 0;
+}
+
+void dist_unique_id(uint8_t out[128]) {
+  ncclUniqueId uid;
+  nccl_check(nccl().getUniqueId(&uid), "ncclGetUniqueId");
+  std::memcpy(out, uid.internal, 128);
+}
+
+}  // namespace nt

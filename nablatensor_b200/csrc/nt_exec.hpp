@@ -1,0 +1,66 @@
+// nt_exec.hpp -- the compiled executable behind an nt_exec handle.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <memory>
+#include <mutex>
+
+#include "nt_internal.hpp"
+
+namespace nt {
+
+void cuda_check(cudaError_t e, const char* what);
+void dist_unique_id(uint8_t out[128]);
+void shard_range(uint64_t total, uint64_t offset, int32_t nranks, int32_t rank, uint64_t* from, uint64_t* count);
+
+struct Exec {
+  std::mutex mu;
+  Tape tape;
+  Plan plan;
+  EmitConfig cfg;
+  std::string source;
+  int device = -1;
+  bool use_disk_cache = true;
+  CUmodule module = nullptr;
+  CUfunction function = nullptr;
+  cudaStream_t stream = nullptr;
+  int sm_count = 0, blocks_per_sm = 0, grid = 0, dyn_smem = 0;
+  int32_t channels = 0;
+  double* d_inputs = nullptr;
+  double* d_partials = nullptr;
+  unsigned int* d_ticket = nullptr;
+  double* d_out = nullptr;
+  double* d_acc = nullptr;
+  double* d_red = nullptr;
+  void* d_gck = nullptr;
+  double* h_stage = nullptr;  // pinned: inputs, then sums
+  std::vector<double> inputs;
+  bool dirty = true;
+  double compile_seconds = 0.0;
+  uint64_t launches = 0;
+  nt_exec_info info{};
+  // multi-GPU
+  void* comm = nullptr;
+  int32_t nranks = 1, rank = 0, dist_timeout_ms = 60000;
+
+  static Exec* create(const nt_tape* tape, const nt_options* opt);
+  ~Exec();
+
+  void bind() const;
+  void load(int max_regs);
+  void upload_inputs_if_dirty();
+  void launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, int accumulate);
+  void replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, double* seconds);
+  void accumulate(uint64_t paths, uint64_t offset, uint64_t seed);
+  void read_accumulator(double* sums, bool reset);
+  void shard(uint64_t total, uint64_t offset, uint64_t* from, uint64_t* count) const;
+  void sharded_enqueue(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk);
+  void sharded(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk, double* sums, double* seconds);
+  void attach(int32_t n, int32_t r, const uint8_t id[128], int32_t timeout_ms);
+  void detach();
+};
+
+}  // namespace nt

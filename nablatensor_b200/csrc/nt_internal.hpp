@@ -1,0 +1,129 @@
+// nt_internal.hpp -- internal types of libnabla_b200 (tape, loop plan, emitter).
+#pragma once
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/nabla_b200.h"
+
+namespace nt {
+
+// An error that crosses no ABI: the C entry points turn it into a status code
+// and a thread-local message.
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& msg) : std::runtime_error(msg), code(c) {}
+};
+
+[[noreturn]] inline void fail(int code, const std::string& msg) { throw Error(code, msg); }
+
+inline bool is_unary(int op) {
+  return op == NT_NEG || op == NT_EXP || op == NT_LOG || op == NT_SQRT || op == NT_ABS;
+}
+inline bool is_binary(int op) {
+  return op == NT_ADD || op == NT_SUB || op == NT_MUL || op == NT_DIV || op == NT_MAX || op == NT_MIN;
+}
+inline bool is_draw(int op) { return op == NT_RANDN || op == NT_RANDU; }
+const char* op_name(int op);
+
+// A validated tape (FlatTape.java:37-79 plus AadTape's stream counts).
+struct Tape {
+  int32_t n = 0;
+  std::vector<int32_t> op, a, b;
+  std::vector<double> c;
+  std::vector<int32_t> input_node, output_node;
+  int32_t n_streams = 1;
+  std::vector<int32_t> normal_count, uniform_count;
+  std::vector<uint8_t> active;  // AadTape.markActive (AadTape.java:70-81)
+  int32_t n_in() const { return (int32_t)input_node.size(); }
+  int32_t n_out() const { return (int32_t)output_node.size(); }
+};
+
+// Copies and validates a caller's tape; throws Error(NT_E_TAPE, ...) on any
+// malformed index, op code or count.
+Tape ingest(const nt_tape* t);
+
+// How a loop-body argument is reached.
+enum RefKind : int8_t { REF_NONE = 0, REF_SAME = 1, REF_CARRY = 2, REF_OUT = 3 };
+struct Ref {
+  RefKind kind = REF_NONE;
+  int32_t idx = -1;  // SAME/CARRY: offset in the unit; OUT: node index outside the loop
+};
+
+struct BodyNode {
+  int32_t op = 0;
+  Ref ra, rb;
+  double c = 0.0;
+  int32_t stream = 0;       // draws
+  int32_t draw_base = 0;    // ordinal in unit 0
+  int32_t draw_stride = 0;  // ordinal increase per unit
+  bool active = false;      // OR over all units
+};
+
+// The step loop of a tape: units [B + u*L, B + (u+1)*L) for u in [0, N).
+struct Loop {
+  bool present = false;
+  int32_t B = -1, L = 0, N = 0;
+  int32_t steps_per_unit = 1;  // tape iterations folded into one unit (RNG pairing)
+  std::vector<BodyNode> body;
+  std::vector<int32_t> carries;     // unit offsets read by the next unit
+  std::vector<int32_t> carry_init;  // per carry: the node feeding unit 0
+  std::vector<int32_t> exits;       // unit offsets read outside the loop (last unit)
+  std::vector<uint8_t> is_carry;    // per offset
+  std::vector<int32_t> carry_slot;  // per offset: index into carries or -1
+  std::vector<uint8_t> is_exit;     // per offset
+  std::vector<int32_t> ckpt;        // carries saved at each segment boundary
+  std::vector<uint8_t> stored;      // per offset: value kept for the reverse sweep
+  std::vector<uint8_t> recompute;   // per offset: recomputed from the segment checkpoint
+  int32_t G = 0;                    // units per segment
+  int32_t K = 0;                    // segments (N = K * G)
+  int32_t end() const { return B + N * L; }
+  bool in(int32_t i) const { return present && i >= B && i < end(); }
+  int32_t off(int32_t i) const { return (i - B) % L; }
+  int32_t unit(int32_t i) const { return (i - B) / L; }
+};
+
+struct Plan {
+  Loop loop;
+  double fwd_flops = 0.0;  // algorithmic, per scenario
+  double rev_flops = 0.0;
+  int32_t stored_per_unit = 0;
+};
+
+struct EmitConfig {
+  bool f32 = false;
+  bool adjoints = true;
+  bool no_loop = false;
+  bool global_ckpt = false;
+  int32_t block = 128;
+  int32_t min_blocks = 0;
+  int32_t seg_units = 0;   // 0 = automatic
+  int32_t target = 0;      // 0 CUDA, 1 host C++
+};
+
+// Finds the step loop and the checkpoint / recompute sets.
+Plan plan_tape(const Tape& t, const EmitConfig& cfg);
+
+// Emits CUDA C (target 0) or host C++ (target 1) for the plan.
+std::string emit(const Tape& t, const Plan& p, const EmitConfig& cfg);
+
+// Number of checkpointed values per thread for this plan (shared/global sizing).
+int32_t ckpt_values(const Plan& p);
+
+extern const char* kDeviceRuntimeSource;  // nt_device_rt.cuh, embedded at build time
+
+// Frozen flop weights of the fp64 transcendentals {exp, log, sqrt, sincos}
+// (nt_flops.cpp), used for the algorithmic flop count of a tape.
+extern const double kFlopWeights[4];
+
+// Runs the device Philox/Box-Muller for the known-answer interface.
+void philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
+                  uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals);
+
+// NVRTC: compile to an sm_100a cubin (cached in memory and on disk).
+std::vector<char> nvrtc_compile(const std::string& source, const std::string& arch, bool use_disk_cache,
+                                double* seconds);
+
+}  // namespace nt

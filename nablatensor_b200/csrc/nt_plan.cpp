@@ -1,0 +1,422 @@
+// nt_plan.cpp -- step-loop detection and the step-wise checkpoint plan.
+//
+// A Monte-Carlo tape is a prologue (inputs, set-up), a body recorded once per
+// time step, and an epilogue (payoff, discount).  Emitting the body once as a
+// rolled loop keeps the kernel small (instruction-cache resident) and lets the
+// reverse sweep work step-wise: the forward loop saves the loop-carried values
+// every G units, and the reverse sweep, segment by segment from the last,
+// restores them, recomputes the segment's units into registers and walks them
+// backwards.  The reference reached long tapes with node-count segments
+// (nablatensor-core/.../AadCheckpointPlan.java:95-172) and the cpu-jit engine
+// with a rolled loop (nablatensor-engine-cpu/.../jit/KernelGenerator.java:536-708);
+// this plan is loop-aware from the start.
+//
+// Detection: a unit of L nodes starting at B repeats N times when, for every
+// offset j, node B+uL+j has the same op (and constant, stream) in every unit
+// and each argument is either the same offset in the same unit, an offset in
+// the previous unit (a carry; unit 0 reads a prologue node instead, the carry's
+// initial value), or one fixed node before B (an invariant).  Nodes after the
+// loop may read only the last unit.
+#include <algorithm>
+#include <cstring>
+#include <map>
+
+#include "nt_internal.hpp"
+
+namespace nt {
+
+namespace {
+
+bool same_double(double x, double y) { return std::memcmp(&x, &y, sizeof x) == 0; }
+
+int nargs(int op) { return is_binary(op) ? 2 : (is_unary(op) ? 1 : 0); }
+
+int32_t arg(const Tape& t, int32_t i, int w) { return w == 0 ? t.a[i] : t.b[i]; }
+
+// Strict shift compatibility of node i with node i+L.
+bool compat(const Tape& t, int32_t i, int32_t L) {
+  const int32_t j = i + L;
+  const int op = t.op[i];
+  if (t.op[j] != op) return false;
+  if (op == NT_INPUT) return false;
+  if (op == NT_CONST) return same_double(t.c[i], t.c[j]);
+  if (is_draw(op)) return t.b[i] == t.b[j] && t.a[j] > t.a[i];
+  for (int w = 0; w < nargs(op); ++w) {
+    const int32_t x = arg(t, i, w), y = arg(t, j, w);
+    if (y != x + L && y != x) return false;
+  }
+  return true;
+}
+
+struct Candidate {
+  int32_t B = -1, L = 0, N = 0, carries = 0;
+};
+
+// Full check of (B, L): returns the number of units N >= 2 that repeat, with
+// outside readers restricted to the last unit, or 0.
+int32_t validate(const Tape& t, int32_t B, int32_t L, int32_t* ncarries) {
+  if (B < 0 || L <= 0 || (int64_t)B + 2 * (int64_t)L > t.n) return 0;
+  std::vector<Ref> ra(L), rb(L);
+  std::vector<int32_t> init(L, -1), stride(L, 0);
+  // Classify from unit 1 (the template).
+  for (int32_t j = 0; j < L; ++j) {
+    const int32_t i1 = B + L + j, i0 = B + j;
+    const int op = t.op[i1];
+    if (t.op[i0] != op || op == NT_INPUT) return 0;
+    if (op == NT_CONST && !same_double(t.c[i0], t.c[i1])) return 0;
+    if (is_draw(op)) {
+      if (t.b[i0] != t.b[i1]) return 0;
+      stride[j] = t.a[i1] - t.a[i0];
+      if (stride[j] <= 0) return 0;
+    }
+    for (int w = 0; w < nargs(op); ++w) {
+      const int32_t x1 = arg(t, i1, w), x0 = arg(t, i0, w);
+      Ref r;
+      if (x1 >= B + L) {
+        r = {REF_SAME, x1 - (B + L)};
+        if (x0 != B + r.idx) return 0;
+      } else if (x1 >= B) {
+        r = {REF_CARRY, x1 - B};
+        if (x0 >= B) return 0;
+        if (init[r.idx] < 0) init[r.idx] = x0;
+        else if (init[r.idx] != x0) return 0;
+      } else {
+        r = {REF_OUT, x1};
+        if (x0 != x1) return 0;
+      }
+      (w == 0 ? ra : rb)[j] = r;
+    }
+  }
+  // Extend over units 2, 3, ...
+  int32_t N = 2;
+  for (;; ++N) {
+    const int64_t base = (int64_t)B + (int64_t)N * L;
+    if (base + L > t.n) break;
+    bool ok = true;
+    for (int32_t j = 0; j < L && ok; ++j) {
+      const int32_t i = (int32_t)base + j, i0 = B + j;
+      const int op = t.op[i];
+      if (op != t.op[i0]) { ok = false; break; }
+      if (op == NT_CONST) { ok = same_double(t.c[i], t.c[i0]); continue; }
+      if (is_draw(op)) {
+        ok = t.b[i] == t.b[i0] && (int64_t)t.a[i] == (int64_t)t.a[i0] + (int64_t)N * stride[j];
+        continue;
+      }
+      for (int w = 0; w < nargs(op) && ok; ++w) {
+        const Ref& r = w == 0 ? ra[j] : rb[j];
+        const int32_t x = arg(t, i, w);
+        if (r.kind == REF_SAME) ok = x == (int32_t)base + r.idx;
+        else if (r.kind == REF_CARRY) ok = x == (int32_t)(base - L) + r.idx;
+        else ok = x == r.idx;
+      }
+    }
+    if (!ok) break;
+  }
+  // Readers after the loop (and outputs) may only see the last unit.
+  for (bool changed = true; changed && N >= 2;) {
+    changed = false;
+    const int32_t end = B + N * L;
+    auto check = [&](int32_t x) {
+      if (x >= B && x < end) {
+        const int32_t u = (x - B) / L;
+        if (u < N - 1) { N = u + 1; changed = true; }
+      }
+    };
+    for (int32_t i = end; i < t.n && !changed; ++i) {
+      const int op = t.op[i];
+      for (int w = 0; w < nargs(op); ++w) check(arg(t, i, w));
+    }
+    for (int32_t o = 0; o < t.n_out() && !changed; ++o) check(t.output_node[o]);
+  }
+  if (N < 2) return 0;
+  if (ncarries) {
+    int32_t c = 0;
+    for (int32_t j = 0; j < L; ++j) c += init[j] >= 0;
+    *ncarries = c;
+  }
+  return N;
+}
+
+std::vector<int32_t> candidate_periods(const Tape& t) {
+  std::vector<int32_t> draws;
+  for (int32_t i = 0; i < t.n; ++i)
+    if (is_draw(t.op[i])) draws.push_back(i);
+  std::vector<int32_t> out;
+  const int32_t nd = (int32_t)draws.size();
+  for (int32_t r = 1; r <= 32 && 4 * r <= nd; ++r) {
+    std::map<int32_t, int32_t> hist;
+    const int32_t lo = nd / 4, hi = std::min(nd - r, lo + 512);
+    for (int32_t k = lo; k < hi; ++k) hist[draws[k + r] - draws[k]]++;
+    int32_t best = 0, bestc = 0;
+    for (auto& kv : hist)
+      if (kv.second > bestc) { best = kv.first; bestc = kv.second; }
+    if (best > 0 && 2 * bestc >= (hi - lo)) out.push_back(best);
+  }
+  for (int32_t L = 1; L <= 64 && 4 * L <= t.n; ++L) out.push_back(L);
+  std::sort(out.begin(), out.end());
+  out.erase(std::unique(out.begin(), out.end()), out.end());
+  return out;
+}
+
+Candidate find_loop(const Tape& t) {
+  Candidate best;
+  for (int32_t L : candidate_periods(t)) {
+    if (3 * (int64_t)L > t.n) continue;
+    // Longest strict run of compat(i, L).
+    int32_t run_s = -1, run_len = 0, cur_s = -1, cur_len = 0;
+    for (int32_t i = 0; i + L < t.n; ++i) {
+      if (compat(t, i, L)) {
+        if (cur_len == 0) cur_s = i;
+        ++cur_len;
+        if (cur_len > run_len) { run_len = cur_len; run_s = cur_s; }
+      } else {
+        cur_len = 0;
+      }
+    }
+    if (run_len < 2 * L) continue;
+    for (int32_t B = std::max(0, run_s - 2 * L); B <= run_s; ++B) {
+      int32_t carries = 0;
+      const int32_t N = validate(t, B, L, &carries);
+      if (N < 3) continue;
+      const int64_t cover = (int64_t)N * L, bcover = (int64_t)best.N * best.L;
+      if (cover > bcover || (cover == bcover && carries < best.carries)) best = {B, L, N, carries};
+    }
+  }
+  return best;
+}
+
+// Fills the unit description for a validated (B, L, N).
+void describe(const Tape& t, Loop& lp) {
+  const int32_t B = lp.B, L = lp.L, N = lp.N;
+  lp.body.assign(L, BodyNode{});
+  lp.is_carry.assign(L, 0);
+  lp.carry_slot.assign(L, -1);
+  lp.is_exit.assign(L, 0);
+  std::vector<int32_t> init(L, -1);
+  for (int32_t j = 0; j < L; ++j) {
+    const int32_t i1 = B + L + j, i0 = B + j;
+    BodyNode& bn = lp.body[j];
+    bn.op = t.op[i1];
+    bn.c = t.c[i1];
+    if (is_draw(bn.op)) {
+      bn.stream = t.b[i1];
+      bn.draw_base = t.a[i0];
+      bn.draw_stride = t.a[i1] - t.a[i0];
+    }
+    for (int w = 0; w < nargs(bn.op); ++w) {
+      const int32_t x1 = arg(t, i1, w), x0 = arg(t, i0, w);
+      Ref r;
+      if (x1 >= B + L) r = {REF_SAME, x1 - (B + L)};
+      else if (x1 >= B) { r = {REF_CARRY, x1 - B}; init[r.idx] = x0; lp.is_carry[r.idx] = 1; }
+      else r = {REF_OUT, x1};
+      (w == 0 ? bn.ra : bn.rb) = r;
+    }
+    uint8_t act = 0;
+    for (int32_t u = 0; u < N && !act; ++u) act |= t.active[B + u * L + j];
+    bn.active = act != 0;
+  }
+  lp.carries.clear();
+  lp.carry_init.clear();
+  for (int32_t k = 0; k < L; ++k)
+    if (lp.is_carry[k]) {
+      lp.carry_slot[k] = (int32_t)lp.carries.size();
+      lp.carries.push_back(k);
+      lp.carry_init.push_back(init[k]);
+    }
+  const int32_t end = B + N * L;
+  auto mark = [&](int32_t x) {
+    if (x >= B && x < end) lp.is_exit[(x - B) % L] = 1;
+  };
+  for (int32_t i = end; i < t.n; ++i)
+    for (int w = 0; w < nargs(t.op[i]); ++w) mark(arg(t, i, w));
+  for (int32_t o = 0; o < t.n_out(); ++o) mark(t.output_node[o]);
+  lp.exits.clear();
+  for (int32_t k = 0; k < L; ++k)
+    if (lp.is_exit[k]) lp.exits.push_back(k);
+}
+
+// Values the reverse sweep of a unit reads (ScalarReplay.java:129-171 rules,
+// restricted to contributions into active arguments as the device sweep does).
+void reverse_reads(const Loop& lp, int32_t j, std::vector<Ref>& out) {
+  const BodyNode& bn = lp.body[j];
+  out.clear();
+  if (!bn.active) return;
+  auto act = [&](const Ref& r) {
+    if (r.kind == REF_SAME || r.kind == REF_CARRY) return lp.body[r.idx].active;
+    return true;  // outside node: activity decided by the tape; reading its value is harmless
+  };
+  const Ref self{REF_SAME, j};
+  switch (bn.op) {
+    case NT_MUL:
+      if (act(bn.ra)) out.push_back(bn.rb);
+      if (act(bn.rb)) out.push_back(bn.ra);
+      break;
+    case NT_DIV:
+      out.push_back(bn.rb);
+      if (act(bn.rb)) out.push_back(self);
+      break;
+    case NT_EXP: case NT_SQRT: out.push_back(self); break;
+    case NT_LOG: case NT_ABS: out.push_back(bn.ra); break;
+    case NT_MAX: case NT_MIN: out.push_back(bn.ra); out.push_back(bn.rb); break;
+    default: break;
+  }
+}
+
+// Algorithmic flop weights per op (frozen; see DESIGN.md "flop convention").
+// Transcendentals count the fp64 flops of the device routine (FMA = 2).
+struct Weights {
+  double add = 1, mul = 1, div = 1, neg = 1, minmax = 1, abs = 1;
+  double exp = 0, log = 0, sqrt = 0, sincos = 0;  // filled from kFlopWeights
+};
+
+}  // namespace
+
+int32_t ckpt_values(const Plan& p) {
+  return p.loop.present ? p.loop.K * (int32_t)p.loop.ckpt.size() : 0;
+}
+
+Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
+  Plan p;
+  Loop& lp = p.loop;
+  if (!cfg.no_loop) {
+    Candidate c = find_loop(t);
+    if (c.N >= 3) {
+      lp.present = true;
+      lp.B = c.B;
+      lp.L = c.L;
+      lp.N = c.N;
+    }
+  }
+  if (lp.present) {
+    // Fold iterations so each unit draws whole Box-Muller pairs: a pair's two
+    // legs must land in the same unit and start at an even ordinal.
+    describe(t, lp);
+    bool odd_stride = false, odd_base = false;
+    for (const BodyNode& bn : lp.body)
+      if (bn.op == NT_RANDN) odd_stride |= (bn.draw_stride & 1) != 0;
+    int32_t U = odd_stride ? 2 : 1;
+    // Smallest normal ordinal per stream in unit 0.
+    std::map<int32_t, int32_t> first;
+    for (const BodyNode& bn : lp.body)
+      if (bn.op == NT_RANDN) {
+        auto it = first.find(bn.stream);
+        if (it == first.end() || bn.draw_base < it->second) first[bn.stream] = bn.draw_base;
+      }
+    for (auto& kv : first) odd_base |= (kv.second & 1) != 0;
+    int32_t B = lp.B, L = lp.L, N = lp.N;
+    if (odd_base && odd_stride) { B += L; N -= 1; }  // peel one iteration into the prologue
+    int32_t units = N / U;
+    // Units per checkpoint segment: a divisor of the unit count close to the
+    // target; otherwise the remainder units are peeled into the epilogue.
+    const int32_t target = cfg.seg_units > 0 ? cfg.seg_units : std::max(1, 8 / U);
+    int32_t G = target;
+    if (units >= 2) {
+      int32_t bestG = -1;
+      for (int32_t g = std::max(1, target - target / 3); g <= target + target / 3 + 1; ++g)
+        if (units % g == 0 && (bestG < 0 || std::abs(g - target) < std::abs(bestG - target))) bestG = g;
+      if (cfg.seg_units > 0) bestG = (units % cfg.seg_units == 0) ? cfg.seg_units : -1;
+      if (bestG > 0) G = bestG;
+    }
+    G = std::max(1, std::min(G, units));
+    const int32_t K = units / G;
+    if (K < 1 || units < 2) {
+      lp = Loop{};
+    } else {
+      lp.B = B;
+      lp.L = L * U;
+      lp.N = K * G;
+      lp.steps_per_unit = U;
+      int32_t nc = 0;
+      const int32_t N2 = validate(t, lp.B, lp.L, &nc);
+      if (N2 < lp.N) {
+        lp = Loop{};
+      } else {
+        describe(t, lp);
+        lp.G = G;
+        lp.K = K;
+      }
+    }
+  }
+  if (lp.present) {
+    const int32_t L = lp.L;
+    // Stored values: everything the reverse of a unit reads from its own unit
+    // or (for unit 0 of a segment) from the previous unit's carries.
+    lp.stored.assign(L, 0);
+    std::vector<uint8_t> carry_read(L, 0);
+    std::vector<Ref> reads;
+    for (int32_t j = 0; j < L; ++j) {
+      reverse_reads(lp, j, reads);
+      for (const Ref& r : reads) {
+        if (r.kind == REF_SAME) lp.stored[r.idx] = 1;
+        else if (r.kind == REF_CARRY) { lp.stored[r.idx] = 1; carry_read[r.idx] = 1; }
+      }
+    }
+    // Recompute closure: nodes needed to regenerate the stored values.
+    std::vector<uint8_t> need(lp.stored);
+    for (bool changed = true; changed;) {
+      changed = false;
+      for (int32_t j = L - 1; j >= 0; --j) {
+        if (!need[j]) continue;
+        const BodyNode& bn = lp.body[j];
+        for (int w = 0; w < nargs(bn.op); ++w) {
+          const Ref& r = w == 0 ? bn.ra : bn.rb;
+          if ((r.kind == REF_SAME || r.kind == REF_CARRY) && !need[r.idx]) { need[r.idx] = 1; changed = true; }
+          if (r.kind == REF_CARRY) carry_read[r.idx] = 1;
+        }
+      }
+    }
+    lp.recompute = need;
+    lp.ckpt.clear();
+    for (int32_t k : lp.carries)
+      if (carry_read[k]) lp.ckpt.push_back(k);
+    p.stored_per_unit = 0;
+    for (int32_t j = 0; j < L; ++j) p.stored_per_unit += lp.stored[j];
+  }
+
+  // Algorithmic flops per scenario (tape ops only; Box-Muller per pair).
+  Weights w;
+  w.exp = kFlopWeights[0];
+  w.log = kFlopWeights[1];
+  w.sqrt = kFlopWeights[2];
+  w.sincos = kFlopWeights[3];
+  double fwd = 0, rev = 0;
+  for (int32_t i = 0; i < t.n; ++i) {
+    const int op = t.op[i];
+    switch (op) {
+      case NT_ADD: case NT_SUB: fwd += w.add; break;
+      case NT_MUL: fwd += w.mul; break;
+      case NT_DIV: fwd += w.div; break;
+      case NT_NEG: fwd += w.neg; break;
+      case NT_MAX: case NT_MIN: fwd += w.minmax; break;
+      case NT_ABS: fwd += w.abs; break;
+      case NT_EXP: fwd += w.exp; break;
+      case NT_LOG: fwd += w.log; break;
+      case NT_SQRT: fwd += w.sqrt; break;
+      case NT_RANDN:
+        // one Box-Muller pair per two normals: log + sqrt + sincos + 6 flops
+        fwd += 0.5 * (w.log + w.sqrt + w.sincos + 6.0);
+        break;
+      case NT_RANDU: fwd += 2.0; break;
+      default: break;
+    }
+    if (!cfg.adjoints || !t.active[i]) continue;
+    const bool aa = (is_unary(op) || is_binary(op)) && t.active[t.a[i]];
+    const bool ab = is_binary(op) && t.active[t.b[i]];
+    switch (op) {
+      case NT_ADD: case NT_SUB: rev += aa + ab; break;             // d += dy
+      case NT_MUL: rev += 2.0 * (aa + ab); break;                  // d += dy*v
+      case NT_DIV: rev += 2.0 * aa + 3.0 * ab; break;              // d += dy/vb ; d -= dy*vi/vb
+      case NT_NEG: rev += aa; break;
+      case NT_EXP: rev += 2.0 * aa; break;
+      case NT_LOG: rev += 2.0 * aa; break;
+      case NT_SQRT: rev += 3.0 * aa; break;
+      case NT_ABS: case NT_MAX: case NT_MIN: rev += aa + ab; break;
+      default: break;
+    }
+  }
+  p.fwd_flops = fwd;
+  p.rev_flops = cfg.adjoints ? rev * t.n_out() : 0.0;
+  return p;
+}
+
+}  // namespace nt

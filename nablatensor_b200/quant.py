@@ -1,0 +1,246 @@
+"""Tape producers for the equity Monte-Carlo products (the L5 front-end).
+
+Restates, node for node, the recording order of
+  nablatensor-quant/.../quant/Products.java:70-161 (european, asian),
+  nablatensor-quant/.../quant/GbmPath.java:48-91 (uniform-grid GBM step),
+  nablatensor-quant/.../quant/ExoticProducts.java:55-75 (smoothed barrier),
+  nablatensor-ops/.../ops/Smooth.java:44-68 (logistic step),
+  nablatensor-quant/.../quant/CorrelatedNormals.java:36-93 (Cholesky mix),
+  nablatensor-core/.../engine/Nabla.java:201-207 (market inputs first, in the
+  market class's field order).
+These run unchanged above the engine boundary in the reference; here they
+produce the tapes the B200 engine replays.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, fields
+from enum import Enum
+from typing import Callable, List, Sequence
+
+import numpy as np
+
+from .tape import AadRecorder, AadTape, ADouble
+
+
+@dataclass(frozen=True)
+class EquityMarket:
+    """EquityMarket.java: field order spot, strike, vol, rate, maturity."""
+    spot: float
+    strike: float
+    vol: float
+    rate: float
+    maturity: float
+
+    @staticmethod
+    def atm_one_year() -> "EquityMarket":
+        return EquityMarket(100.0, 100.0, 0.20, 0.03, 1.0)
+
+    def validated(self) -> "EquityMarket":
+        if not (self.vol >= 0.0) or not (self.maturity >= 0.0) or not (self.spot > 0.0) or not (self.strike > 0.0):
+            raise ValueError(f"need spot>0, strike>0, vol>=0, maturity>=0; got {self}")
+        return self
+
+
+class Inputs:
+    """Nabla.Inputs: one INPUT node per market field, recorded first."""
+
+    def __init__(self, rec: AadRecorder, market):
+        self._names = [f.name for f in fields(market)]
+        self._nodes = [rec.input(n, float(getattr(market, n))) for n in self._names]
+
+    def of(self, name: str) -> ADouble:
+        return self._nodes[self._names.index(name)]
+
+
+class TimeGrid:
+    """TimeGrid.uniform(n): n equal fractions 1.0 / n."""
+
+    def __init__(self, fractions: Sequence[float], uniform: bool):
+        self.fractions = list(fractions)
+        self.uniform = uniform
+
+    @staticmethod
+    def uniform_grid(n: int) -> "TimeGrid":
+        if n < 1:
+            raise ValueError(f"steps must be >= 1, got {n}")
+        return TimeGrid([1.0 / n] * n, True)
+
+    def steps(self) -> int:
+        return len(self.fractions)
+
+
+class GbmPath:
+    """GbmPath (GbmPath.java:48-91)."""
+
+    def __init__(self, rec: AadRecorder, rate: ADouble, vol: ADouble, grid: TimeGrid, maturity: ADouble):
+        n = grid.steps()
+        half_var = rate.sub(vol.mul(vol).mul(0.5))
+        if grid.uniform:
+            dt = maturity.mul(grid.fractions[0])
+            d = half_var.mul(dt)
+            s = vol.mul(dt.sqrt())
+            self.drift = [d] * n
+            self.diffusion = [s] * n
+        else:
+            self.drift, self.diffusion = [], []
+            for i in range(n):
+                dt = maturity.mul(grid.fractions[i])
+                self.drift.append(half_var.mul(dt))
+                self.diffusion.append(vol.mul(dt.sqrt()))
+
+    def step(self, spot: ADouble, z: ADouble, i: int) -> ADouble:
+        return spot.mul(self.drift[i].add(self.diffusion[i].mul(z)).exp())
+
+
+class OptionType(Enum):
+    CALL = 1
+    PUT = 0
+
+
+class Barrier(Enum):
+    """BarrierEnum order: UP_OUT, UP_IN, DOWN_OUT, DOWN_IN."""
+    UP_OUT = 0
+    UP_IN = 1
+    DOWN_OUT = 2
+    DOWN_IN = 3
+
+
+class _Sim:
+    """The shared set-up of Products / ExoticProducts (their private Sim)."""
+
+    def __init__(self, rec: AadRecorder, inp: Inputs, grid: TimeGrid):
+        self.spot = inp.of("spot")
+        self.strike = inp.of("strike")
+        self.rate = inp.of("rate")
+        self.maturity = inp.of("maturity")
+        self.model = GbmPath(rec, self.rate, inp.of("vol"), grid, self.maturity)
+
+    def discount(self, payoff: ADouble) -> ADouble:
+        return payoff.mul(self.rate.neg().mul(self.maturity).exp())
+
+
+def _intrinsic(kind: OptionType, underlying: ADouble, strike: ADouble) -> ADouble:
+    diff = underlying.sub(strike) if kind == OptionType.CALL else strike.sub(underlying)
+    return diff.max(0.0)
+
+
+class Smooth:
+    """Smooth.java:44-68."""
+
+    @staticmethod
+    def step(rec: AadRecorder, x: ADouble, width: float) -> ADouble:
+        if not (width > 0.0) or math.isinf(width):
+            raise ValueError("width must be positive and finite")
+        e = x.div(width).neg().exp()
+        return rec.constant(1.0).div(e.add(1.0))
+
+    @staticmethod
+    def gt(rec: AadRecorder, a: ADouble, level, width: float) -> ADouble:
+        return Smooth.step(rec, a.sub(level), width)
+
+    @staticmethod
+    def lt(rec: AadRecorder, a: ADouble, level, width: float) -> ADouble:
+        if isinstance(level, ADouble):
+            return Smooth.step(rec, level.sub(a), width)
+        return Smooth.step(rec, a.neg().add(level), width)
+
+
+Product = Callable[[AadRecorder, Inputs, TimeGrid], None]
+
+
+class Products:
+    """Products.java: European and arithmetic-average Asian options."""
+
+    @staticmethod
+    def european(kind: OptionType = OptionType.CALL) -> Product:
+        def record(rec, inp, grid):
+            sim = _Sim(rec, inp, grid)
+            terminal = sim.spot
+            for t in range(grid.steps()):
+                terminal = sim.model.step(terminal, rec.randn(), t)
+            rec.output(sim.discount(_intrinsic(kind, terminal, sim.strike)))
+        return record
+
+    @staticmethod
+    def asian(kind: OptionType = OptionType.CALL) -> Product:
+        def record(rec, inp, grid):
+            sim = _Sim(rec, inp, grid)
+            path = sim.spot
+            total = rec.constant(0.0)
+            for t in range(grid.steps()):
+                path = sim.model.step(path, rec.randn(), t)
+                total = total.add(path)
+            average = total.div(float(grid.steps()))
+            rec.output(sim.discount(_intrinsic(kind, average, sim.strike)))
+        return record
+
+    @staticmethod
+    def asian_call() -> Product:
+        return Products.asian(OptionType.CALL)
+
+    @staticmethod
+    def european_call() -> Product:
+        return Products.european(OptionType.CALL)
+
+
+class ExoticProducts:
+    """ExoticProducts.createBarrier (ExoticProducts.java:55-75)."""
+
+    @staticmethod
+    def barrier(kind: OptionType, barrier_kind: Barrier, level: float, width: float) -> Product:
+        def record(rec, inp, grid):
+            sim = _Sim(rec, inp, grid)
+            path = sim.spot
+            survival = rec.constant(1.0)
+            up = barrier_kind in (Barrier.UP_OUT, Barrier.UP_IN)
+            for t in range(grid.steps()):
+                path = sim.model.step(path, rec.randn(), t)
+                not_breached = Smooth.lt(rec, path, level, width) if up else Smooth.gt(rec, path, level, width)
+                survival = survival.mul(not_breached)
+            vanilla = path.sub(sim.strike).max(0.0) if kind == OptionType.CALL else sim.strike.sub(path).max(0.0)
+            knock_out = barrier_kind in (Barrier.UP_OUT, Barrier.DOWN_OUT)
+            alive = survival if knock_out else rec.constant(1.0).sub(survival)
+            rec.output(sim.discount(vanilla.mul(alive)))
+        return record
+
+
+def record_model(market, product: Product, grid: TimeGrid) -> AadTape:
+    """Nabla.model(market, (rec, in) -> product.record(rec, in, grid)).tape()."""
+    def body(rec):
+        product(rec, Inputs(rec, market), grid)
+    return AadRecorder.record(body)
+
+
+def asian_tape(steps: int = 252, market: EquityMarket = None) -> AadTape:
+    return record_model(market or EquityMarket.atm_one_year(), Products.asian_call(), TimeGrid.uniform_grid(steps))
+
+
+def european_tape(steps: int = 1, market: EquityMarket = None) -> AadTape:
+    return record_model(market or EquityMarket.atm_one_year(), Products.european_call(), TimeGrid.uniform_grid(steps))
+
+
+def barrier_tape(steps: int = 252, level: float = 80.0, width: float = 1.0, kind: Barrier = Barrier.DOWN_IN,
+                 option: OptionType = OptionType.CALL, market: EquityMarket = None) -> AadTape:
+    return record_model(market or EquityMarket.atm_one_year(), ExoticProducts.barrier(option, kind, level, width),
+                        TimeGrid.uniform_grid(steps))
+
+
+# ---- generic tapes used by the conformance tests ---------------------------------
+
+def every_op(rec: AadRecorder) -> None:
+    """A tape touching all 15 ops (the shape of AadOpConformanceTest.everyOp)."""
+    x = rec.input("x", 1.3)
+    y = rec.input("y", 0.7)
+    z = rec.randn()
+    u = rec.randu()
+    a = x.add(y).sub(0.1)
+    b = x.mul(y).div(x.add(0.5))
+    c = a.neg().exp().add(b.abs())
+    d = c.add(1.0).log().sqrt()
+    e = d.max(z.mul(0.01)).min(x.mul(2.0))
+    rec.output(e.add(u.mul(y)))
+
+
+__all__ = ["EquityMarket", "TimeGrid", "GbmPath", "OptionType", "Barrier", "Smooth", "Products", "ExoticProducts",
+           "Inputs", "record_model", "asian_tape", "european_tape", "barrier_tape", "every_op"]

@@ -1,0 +1,144 @@
+"""The C ABI: symbols, error statuses, NVRTC compile -- no GPU needed."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from nablatensor_b200 import _lib, quant
+from nablatensor_b200.tape import AadRecorder
+
+from tapes import every_op_tape, named_streams, multi_output
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    text = open(os.path.join(ROOT, "include", "nabla_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(nt_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(ntlib):
+    declared = _declared()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(ntlib, name), name
+    assert sorted(_lib.SIGNATURES) == declared
+
+
+def test_version_and_device_probe_never_fault(ntlib):
+    assert ntlib.nt_version() == 1
+    n = _lib.device_count()  # 0 on a CPU-only machine, no exception
+    assert n >= 0
+
+
+def _compile_status(tape, **opts):
+    s, keep = _lib.tape_struct(tape)
+    o = _lib.options_struct(**opts)
+    h = ctypes.c_void_p()
+    rc = _lib.lib().nt_compile(ctypes.byref(s), ctypes.byref(o), ctypes.byref(h))
+    msg = _lib.lib().nt_last_error().decode()
+    if rc == 0:
+        _lib.lib().nt_destroy(h)
+    return rc, msg
+
+
+def _tape_arrays(tape):
+    return {k: np.array(getattr(tape, k)) for k in
+            ("op", "arg_a", "arg_b", "constant", "input_node", "output_node", "normal_count", "uniform_count")}
+
+
+class _Raw:
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def _malformed(mutate):
+    t = quant.asian_tape(8)
+    d = _tape_arrays(t)
+    mutate(d)
+    return _Raw(**d)
+
+
+@pytest.mark.parametrize("mutate,needle", [
+    (lambda d: d["op"].__setitem__(20, 99), "unknown op"),
+    (lambda d: d["arg_a"].__setitem__(20, 10_000), "out of order"),
+    (lambda d: d["arg_b"].__setitem__(22, 22), "out of order"),
+    (lambda d: d["arg_a"].__setitem__(0, 7), "input index out of range"),
+    (lambda d: d["arg_a"].__setitem__(15, 3), "draw ordinals"),
+    (lambda d: d["arg_b"].__setitem__(15, 4), "stream out of range"),
+    (lambda d: d["output_node"].__setitem__(0, 10**6), "out of range"),
+    (lambda d: d["input_node"].__setitem__(1, 5), "is not INPUT"),
+    (lambda d: d["normal_count"].__setitem__(0, 3), "normal_count"),
+])
+def test_malformed_tapes_are_rejected_before_emission(ntlib, mutate, needle):
+    """ingest() checks every index (the reference trusted its recorder)."""
+    raw = _malformed(mutate)
+    s, keep = _lib.tape_struct(raw)
+    o = _lib.options_struct()
+    n = ctypes.c_size_t(0)
+    rc = _lib.lib().nt_emit_source(ctypes.byref(s), ctypes.byref(o), 0, None, 0, ctypes.byref(n))
+    assert rc == _lib.NT_E_TAPE
+    assert needle in _lib.lib().nt_last_error().decode()
+
+
+def test_invalid_arguments(ntlib):
+    L = _lib.lib()
+    assert L.nt_compile(None, None, None) == _lib.NT_E_INVALID_ARG
+    assert L.nt_replay(None, 1, 0, 0, None, None) == _lib.NT_E_STATE
+    assert "closed" in L.nt_last_error().decode()
+    L.nt_destroy(None)  # no-op
+    f, c = ctypes.c_uint64(), ctypes.c_uint64()
+    assert L.nt_shard_range(10, 0, 0, 0, ctypes.byref(f), ctypes.byref(c)) == _lib.NT_E_INVALID_ARG
+    with pytest.raises(_lib.NablaError) as e:
+        _lib.emit_source(quant.asian_tape(4), target=2)
+    assert e.value.code == _lib.NT_E_INVALID_ARG
+
+
+def test_bad_block_size_is_an_argument_error(ntlib):
+    rc, msg = _compile_status(quant.asian_tape(4), block=100)
+    # on a CPU box the device probe may fail first; either way no fault
+    assert rc in (_lib.NT_E_INVALID_ARG, _lib.NT_E_CUDA)
+
+
+@pytest.mark.parametrize("f32", [False, True])
+@pytest.mark.parametrize("make", [lambda: quant.asian_tape(252), lambda: quant.barrier_tape(252), every_op_tape,
+                                  lambda: named_streams(16), lambda: multi_output(40)])
+def test_emitted_kernels_compile_for_sm100a(ntlib, make, f32):
+    src = _lib.emit_source(make(), target=0, precision=0 if f32 else 1)
+    assert "nt_replay_kernel" in src and "__launch_bounds__" in src
+    assert _lib.nvrtc_check(src) > 1000
+
+
+def test_nvrtc_errors_are_reported(ntlib):
+    with pytest.raises(_lib.NablaError) as e:
+        _lib.nvrtc_check("extern \"C\" __global__ void k() { this is not C++; }")
+    assert e.value.code == _lib.NT_E_NVRTC
+    assert "NVRTC compile failed" in str(e.value)
+
+
+def test_shard_ranges_tile_the_range(ntlib):
+    for total in (1, 7, 2_000_000, 10**9 + 3):
+        for n in (1, 2, 3, 8):
+            cur = 123
+            for r in range(n):
+                f, c = _lib.shard_range(total, 123, n, r)
+                assert f == cur
+                cur += c
+            assert cur == 123 + total
+
+
+def test_inputs_without_a_device_fail_loudly(ntlib):
+    """No CPU fallback: compiling on a machine without a B200 is an error."""
+    if _lib.device_count() > 0:
+        pytest.skip("a GPU is present")
+    rc, msg = _compile_status(quant.asian_tape(8))
+    assert rc != 0 and msg
+
+
+def test_recorded_tapes_round_trip_through_the_abi(ntlib):
+    t = AadRecorder.record(lambda rec: rec.output(rec.input("x", 1.0).mul(2.0)))
+    src = _lib.emit_source(t, target=1)
+    assert "nt_host_replay" in src

@@ -1,0 +1,115 @@
+"""The emitter's scenario code, compiled for the host, against the oracle.
+
+nt_emit_source(target=1) emits exactly the per-scenario code the CUDA kernel
+runs (loop detection, step-wise checkpoints, segment recompute, reverse
+sweep), wrapped in a sequential host loop.  Built with g++ without FMA
+contraction and linked against the same libm as the oracle, it must
+reproduce the oracle's sums BIT FOR BIT: any mistake in the loop plan, the
+checkpoint slots, the recompute set or the adjoint order shows up as a
+difference.  (Two carries fed by the same initial node accumulate that
+node's adjoint in a different order than the interpreter; those tapes are
+compared at 1e-14.)
+"""
+import numpy as np
+import pytest
+
+from nablatensor_b200 import _lib, quant
+from oracle.oracle import FlatTape
+
+from conftest import host_kernel
+from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, odd_steps_asian,
+                   random_branching)
+
+ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
+
+
+def _run(oracle_mod, tape, inputs, paths, off, seed, rtol=0.0, f32=False, adjoints=True, **opts):
+    src = _lib.emit_source(tape, target=1, precision=0 if f32 else 1, adjoints=adjoints, **opts)
+    run = host_kernel(src)
+    channels = tape.output_count() * (2 + tape.input_count())
+    got = run(inputs, paths, off, seed, channels)
+    want = oracle_mod.replay(FlatTape.of(tape), inputs, paths, off, seed, f32=f32, adjoints=adjoints,
+                             threads=1).sums
+    if not adjoints:
+        stride = 2 + tape.input_count()
+        keep = [o * stride + k for o in range(tape.output_count()) for k in (0, 1)]
+        got, want = got[keep], want[keep]
+    if rtol == 0.0:
+        np.testing.assert_array_equal(got, want)
+    else:
+        np.testing.assert_allclose(got, want, rtol=rtol, atol=0)
+    return src
+
+
+@pytest.mark.parametrize("seg_units", [0, 1, 2, 3, 6, 7, 9, 14, 63])
+def test_asian_loop_is_bit_exact(oracle_mod, seg_units):
+    src = _run(oracle_mod, quant.asian_tape(252), ATM, 3_000, 0x1_0000_0003, 0x1234_5678_FEDC_BA98,
+               seg_units=seg_units)
+    assert "step loop: 126 units" in src
+
+
+def test_asian_straight_line_is_bit_exact(oracle_mod):
+    src = _run(oracle_mod, quant.asian_tape(64), ATM, 2_000, 7, 42, flags=_lib.NT_FLAG_NO_LOOP)
+    assert "step loop" not in src
+
+
+@pytest.mark.parametrize("steps", [3, 4, 5, 31, 64])
+def test_asian_odd_and_short_loops(oracle_mod, steps):
+    _run(oracle_mod, odd_steps_asian(steps), ATM, 2_000, 11, 99)
+
+
+def test_asian_bumped_inputs(oracle_mod):
+    _run(oracle_mod, quant.asian_tape(252), [101.0, 97.0, 0.31, 0.01, 2.0], 1_000, 0, 42)
+
+
+@pytest.mark.parametrize("steps", [1, 252])
+def test_european(oracle_mod, steps):
+    _run(oracle_mod, quant.european_tape(steps), ATM, 5_000, 0, 20260830)
+
+
+@pytest.mark.parametrize("kind", list(quant.Barrier))
+def test_barrier_kinds(oracle_mod, kind):
+    _run(oracle_mod, quant.barrier_tape(60, 80.0 if "DOWN" in kind.name else 120.0, 1.0, kind), ATM, 2_000, 3, 42)
+
+
+def test_barrier_config_tape(oracle_mod):
+    _run(oracle_mod, quant.barrier_tape(252), ATM, 1_000, 0, 42)
+
+
+def test_lookback_max_min_rules(oracle_mod):
+    _run(oracle_mod, lookback(64, True), ATM, 2_000, 0, 5, rtol=1e-14)
+    _run(oracle_mod, lookback(64, False), ATM, 2_000, 0, 5, rtol=1e-14)
+
+
+def test_random_branching_tape(oracle_mod):
+    _run(oracle_mod, random_branching(24), [1.2, 0.1], 4_000, 0x1_0000_0003, 42)
+    _run(oracle_mod, random_branching(24), [1.5, 0.1], 4_000, 0x1_0000_0003, 0x1234_5678_FEDC_BA98)
+
+
+def test_every_op_tape(oracle_mod):
+    _run(oracle_mod, every_op_tape(), [1.3, 0.7], 20_000, 0, 0x5EED5)
+
+
+def test_named_streams_and_uniforms(oracle_mod):
+    _run(oracle_mod, named_streams(16), [100.0, 0.2], 5_000, 0, 0xC0FFEE)
+
+
+def test_multi_output(oracle_mod):
+    _run(oracle_mod, multi_output(40), [100.0, 0.25], 3_000, 0, 17)
+
+
+def test_price_only(oracle_mod):
+    _run(oracle_mod, quant.asian_tape(252), ATM, 1_000, 0, 42, adjoints=False)
+
+
+def test_fp32_host_build_tracks_the_fp32_oracle(oracle_mod):
+    # fp32 evaluates each node in float; the oracle evaluates in double and
+    # rounds each stored value, so compound adjoint rules and libm's float
+    # functions differ in the last bits.
+    _run(oracle_mod, fp32_asian_50(50), [100.0, 0.2], 5_000, 0, 0xA51A17, rtol=2e-6, f32=True)
+
+
+def test_loop_plan_reported_for_config_tapes(ntlib):
+    src = _lib.emit_source(quant.barrier_tape(252), target=0, precision=0)
+    assert "step loop: 126 units of 32 nodes (2 steps each)" in src
+    assert "nt_normal_pair32" in src

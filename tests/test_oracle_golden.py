@@ -1,0 +1,124 @@
+"""The oracle against the reference's own golden results and generator rules.
+
+Golden values (the reference's scalar `cpu` engine, JDK 25, 16 threads):
+  G1  docs/validation.md:56-63             Asian call, 252 steps, 1,000,000 paths, seed 42
+  G2  docs/examples/asian-greeks.md:43-46  the same at 2,000,000 paths (all engines agree)
+Both sit in tests/golden/reference_docs.json.  Reproducing them to every
+printed digit needs all 2.5e8 generator draws, the Box-Muller legs, the
+1536-node forward sweep and the adjoint rules to be right.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+ATM = [100.0, 100.0, 0.20, 0.03, 1.0]  # spot, strike, vol, rate, maturity
+
+
+def _docs():
+    with open(os.path.join(GOLDEN, "reference_docs.json")) as f:
+        return json.load(f)
+
+
+def _check_digits(got, want, digits):
+    # `want` is printed with `digits` significant digits: agree to half an ulp of that print.
+    tol = 0.5 * 10 ** (np.floor(np.log10(abs(want))) - (digits - 1))
+    assert abs(got - want) <= tol * 1.0000001, (got, want, tol)
+
+
+def test_g1_asian_1m_matches_validation_md(oracle_mod):
+    O = oracle_mod
+    g = _docs()["G1"]
+    r = O.replay(O.asian_tape(252), ATM, 1_000_000, 0, 42)
+    vals = {"price": r.value[0], "delta": r.gradients[0][0], "dV/dK": r.gradients[0][1],
+            "vega": r.gradients[0][2], "rho": r.gradients[0][3], "dV/dT": r.gradients[0][4]}
+    for name, (want, digits) in g["values"].items():
+        _check_digits(vals[name], want, digits)
+
+
+def test_g2_asian_2m_matches_asian_greeks_md(oracle_mod):
+    O = oracle_mod
+    g = _docs()["G2"]
+    r = O.replay(O.asian_tape(252), ATM, 2_000_000, 0, 42)
+    vals = {"price": r.value[0], "delta": r.gradients[0][0], "vega": r.gradients[0][2], "rho": r.gradients[0][3]}
+    for name, (want, digits) in g["values"].items():
+        _check_digits(vals[name], want, digits)
+
+
+def test_asian_tape_shape_matches_readme(oracle_mod):
+    """README.md:76 -- the 252-step Asian tape has 1536 nodes; 1279 are active."""
+    t = oracle_mod.asian_tape(252)
+    assert t.n == 1536
+    assert int(t.active().sum()) == 1279
+    hist = np.bincount(t.op, minlength=15)
+    # INPUT 5, CONST 5, RANDN 252, ADD 504, SUB 2, MUL 511, DIV 1, NEG 1, EXP 253, SQRT 1, MAX 1
+    assert list(hist) == [5, 5, 252, 0, 504, 2, 511, 1, 1, 253, 0, 1, 1, 0, 0]
+
+
+def test_barrier_tape_shape_matches_readme(oracle_mod):
+    """README.md:86 -- the 252-step barrier tape has 4057 nodes."""
+    t = oracle_mod.barrier_tape(252, True, "DOWN_IN", 80.0, 1.0)
+    assert t.n == 4057
+
+
+def test_exact_and_plain_summation_agree_closely(oracle_mod):
+    O = oracle_mod
+    t = O.asian_tape(32)
+    a = O.replay(t, ATM, 20_000, 5, 7, threads=3)
+    b = O.replay(t, ATM, 20_000, 5, 7, threads=3, exact=True)
+    np.testing.assert_allclose(a.sums, b.sums, rtol=1e-12)
+
+
+def test_thread_split_changes_only_rounding(oracle_mod):
+    O = oracle_mod
+    t = O.asian_tape(16)
+    one = O.replay(t, ATM, 9_999, 0x100000003, 0x12345678FEDCBA98, threads=1, exact=True)
+    many = O.replay(t, ATM, 9_999, 0x100000003, 0x12345678FEDCBA98, threads=7, exact=True)
+    np.testing.assert_allclose(one.sums, many.sums, rtol=1e-15)
+
+
+def test_stream_keys_fold_high_bits(oracle_mod):
+    """Philox.java:45-54: lo = path ^ seed (low words), hi = high words."""
+    O = oracle_mod
+    path, seed = 0x1_0000_0003, 0x1234_5678_FEDC_BA98
+    w_direct = O.philox(0x0000_0003 ^ 0xFEDC_BA98, (0x1 ^ 0x1234_5678) ^ 5, 0x1BD11BDA)
+    assert O.normal_words(path, seed, 0, 5) == w_direct
+    # A named stream s != 0 mixes s * 0x9E3779B1 into the high word only.
+    s = 3
+    hi = (0x1 ^ 0x1234_5678) ^ ((s * 0x9E3779B1) & 0xFFFFFFFF)
+    assert O.normal_words(path, seed, s, 5) == O.philox(0x0000_0003 ^ 0xFEDC_BA98, hi ^ 5, 0x1BD11BDA)
+
+
+def test_normal_legs_share_one_block(oracle_mod):
+    O = oracle_mod
+    for k in range(0, 20, 2):
+        w = O.normal_words(9, 42, 0, k // 2)
+        u1 = (w[0] + 0.5) * 2.3283064365386963e-10
+        u2 = (w[1] + 0.5) * 2.3283064365386963e-10
+        r = np.sqrt(-2.0 * np.log(u1))
+        assert O.normal(9, 42, 0, k) == pytest.approx(r * np.cos(6.283185307179586 * u2), rel=1e-15)
+        assert O.normal(9, 42, 0, k + 1) == pytest.approx(r * np.sin(6.283185307179586 * u2), rel=1e-15)
+
+
+def test_uniform_is_tagged_and_in_unit_interval(oracle_mod):
+    O = oracle_mod
+    us = np.array([O.uniform(p, 0xC0FFEE, 0, k) for p in range(200) for k in range(5)])
+    assert us.min() > 0.0 and us.max() < 1.0
+    # The uniform counter is tagged 0x40000000: uniform k never equals normal pair k's first word.
+    for k in range(5):
+        w = O.philox(7 ^ 0xC0FFEE, 0 ^ (k | 0x40000000), 0x1BD11BDA)
+        assert O.uniform(7, 0xC0FFEE, 0, k) == (w[0] + 0.5) * 2.3283064365386963e-10
+
+
+def test_philox_fixture_matches_restatement(oracle_mod):
+    """tests/golden/philox_u32.json was generated from the restatement by
+    tests/golden/make_golden.py; it is the fixture the GPU words are checked
+    against, so it must stay in step with the oracle."""
+    O = oracle_mod
+    with open(os.path.join(GOLDEN, "philox_u32.json")) as f:
+        fx = json.load(f)
+    for case in fx["cases"]:
+        for q, pair in enumerate(case["words"]):
+            assert tuple(pair) == O.normal_words(case["path"], case["seed"], case["stream"], case["pair0"] + q)
