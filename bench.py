@@ -1,0 +1,292 @@
+#!/usr/bin/env python
+"""Benchmark: replay of the fp64 252-step Asian-call valuation tape with value
++ 5 Greeks from one adjoint sweep, 1e9 scenarios per step,
+scenario ranges sharded across the GPUs with one NCCL all-reduce of the
+7 fp64 accumulators.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Prints one JSON line on rank 0.  `value` is whole-job scenarios/s timed with
+CUDA events on the engine's stream (inputs resident, max over ranks); `e2e`
+is the same metric through the C ABI with host inputs and a host read of the
+sums every step; `roofline` relates the replay kernel's algorithmic fp64
+flops to the measured DFMA peak; `cpu_baseline` is the CPU oracle (a port of
+the reference's scalar `cpu` engine) on a bounded sample on this host.
+`--impl reference` times that CPU oracle alone on all host threads: the
+reference is Java and cannot run here (no JVM).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "scenarios/s (value+all Greeks, one adjoint sweep) at 1/2/4/8 B200; % FP64 peak"
+ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
+SEED = 42
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(index)], stdout=self.out,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.out.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                mhz, mmax, watts = float(r[1]), float(r[2]), float(r[3])
+            except ValueError:
+                continue
+            mx = mmax
+            if watts > 250.0:  # under load
+                sm.append(mhz)
+                for name, flag in zip(names, r[5:9]):
+                    if flag.strip().lower() == "active":
+                        reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples_under_load": len(sm)}
+
+
+def cpu_baseline(paths: int, threads: int = 0) -> dict:
+    """The CPU oracle (port of ScalarReplay + Philox) on all host threads."""
+    from oracle import oracle as O
+    t = O.asian_tape(252)
+    cores = threads or os.cpu_count()
+    O.replay(t, ATM, 10_000, 0, SEED, threads=cores)  # warm
+    t0 = time.perf_counter()
+    O.replay(t, ATM, paths, 0, SEED, threads=cores)
+    secs = time.perf_counter() - t0
+    return {"value": paths / secs, "unit": "scenarios/s", "cores": cores, "kind": "port",
+            "sample": f"{paths} scenarios of the 252-step Asian fp64 tape (value + 5 Greeks), seed {SEED}, "
+                      f"scalar interpreter on {cores} threads, {secs:.2f} s"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    t = O.asian_tape(252)
+    cores = os.cpu_count()
+    sample = args.cpu_sample
+    for w in range(args.warmup):
+        O.replay(t, ATM, max(10_000, sample // 10), w * sample, SEED, threads=cores)
+    times = []
+    for k in range(args.steps):
+        t0 = time.perf_counter()
+        O.replay(t, ATM, sample, k * sample, SEED, threads=cores)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps * sample / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "scenarios/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "asian_call_fp64_252steps_value+5greeks (BASELINE config 3 tape; CPU sample per step)",
+                   "paths_per_step": sample, "seed": SEED},
+        "cpu_baseline": {"value": value, "unit": "scenarios/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} scenarios per step; reference is Java (no JVM on this host), "
+                                   f"timed: C restatement of its scalar `cpu` engine"},
+        "e2e": {"value": value, "unit": "scenarios/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+    from nablatensor_b200 import _lib, quant
+    from nablatensor_b200.engine import AadOptions, AadResult, CudaAadEngine, PrecisionEnum, dist_unique_id
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    tape = quant.asian_tape(252)
+    ex = CudaAadEngine(device=local_rank).compile(tape, AadOptions(precision=PrecisionEnum.FLOAT64))
+    info = ex.info()
+    if world > 1:
+        uid = [dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ex.distAttach(world, rank, uid[0], timeout_ms=120_000)
+    peak64 = _lib.fma_peak(local_rank, True)
+
+    total = int(args.paths)
+    chunk = int(args.chunk)
+    first, mine = _lib.shard_range(total, 0, world, rank)
+    launches_per_step = -(-mine // chunk) if chunk > 0 else 1
+    h = ex._handle()
+    stream = torch.cuda.ExternalStream(ex.stream_handle(), device=torch.device("cuda", local_rank))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    sums = np.zeros(info["channels"], dtype=np.float64)
+
+    def step(offset):
+        _lib.check(_lib.lib().nt_replay_sharded_async(h, total, offset, SEED, chunk))
+
+    for _ in range(args.warmup):
+        step(0)
+        _lib.check(_lib.lib().nt_accumulator_read(h, _lib.ptr(sums, ctypes.c_double), 1))
+    barrier()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank)
+    barrier()
+    with torch.cuda.stream(stream):
+        for k in range(args.steps):
+            flush.zero_()  # L2 flush between timed steps, outside the events
+            starts[k].record(stream)
+            step(0)
+            ends[k].record(stream)
+    stream.synchronize()
+    clk = clocks.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    _lib.check(_lib.lib().nt_accumulator_read(h, _lib.ptr(sums, ctypes.c_double), 1))
+    my_total_ms = sum(step_ms)
+    total_ms = max_over_ranks(my_total_ms)
+    value = args.steps * total / (total_ms * 1e-3)
+    res = AadResult.from_sums(sums, tape, total, 0.0)
+
+    # ---- end to end through the C ABI: host inputs in, host sums out -----------
+    barrier()
+    e2e_times = []
+    for k in range(args.steps):
+        barrier()
+        t0 = time.perf_counter()
+        ex.setInputs(ATM)  # host -> device copy of the 5 inputs
+        r = ex.replaySharded(total, 0, SEED, chunk)  # launches + all-reduce + device -> host sums
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_total = max_over_ranks(sum(e2e_times))
+    e2e_value = args.steps * total / e2e_total
+
+    # ---- roofline of the replay kernel ------------------------------------------
+    flops_per_scen = info["fwd_flops"] + info["rev_flops"]
+    kernel_s = (my_total_ms * 1e-3) / (args.steps * launches_per_step)
+    paths_per_launch = mine / launches_per_step
+    achieved = flops_per_scen * paths_per_launch / kernel_s / 1e12
+    roofline = {"bound": "fp64", "achieved": achieved, "peak": peak64, "unit": "TFLOP/s", "frac": achieved / peak64,
+                "peak_source": "measured DFMA peak on this GPU (nt_fma_peak, of measured)",
+                "flops_per_scenario": flops_per_scen, "traffic": _profiled_traffic(paths_per_launch)}
+
+    line = None
+    if rank == 0:
+        cpu = cpu_baseline(args.cpu_sample) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": "scenarios/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "BASELINE config 3: fp64 Asian call, GBM S0=K=100 sigma=0.2 r=0.03 T=1, "
+                                   "252 steps, value + 5 Greeks from one adjoint sweep, 1e9 scenarios per step, "
+                                   "seed 42, shards + 1 NCCL all-reduce of 7 fp64",
+                       "paths_per_step": total, "chunk_paths": chunk, "l2": "flushed between timed steps "
+                       "(256 MiB write); inputs are 40 bytes", "kernel": {k: info[k] for k in (
+                           "registers", "local_bytes", "blocks_per_sm", "grid", "loop_units", "seg_units",
+                           "segments", "ckpt_slots", "stored_per_unit")},
+                       "price": res.value(), "greeks": dict(zip(tape.input_names, map(float, res.gradients())))},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "scenarios/s", "h2d_bytes_per_step": 8 * len(ATM),
+                    "d2h_bytes_per_step": 8 * info["channels"]},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clk,
+        }
+    if world > 1:
+        ex.distDetach()
+        dist.barrier()
+        dist.destroy_process_group()
+    ex.close()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def _profiled_traffic(paths_per_launch: float):
+    """DRAM bytes per launch from the committed ncu summary, scaled by the
+    scenarios one launch processes (null when no capture is committed)."""
+    path = os.path.join(ROOT, "profiles", "asian_fp64_replay_ncu.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_scenario:"):
+                return float(line.split(":", 1)[1]) * paths_per_launch
+    except OSError:
+        pass
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--paths", type=float, default=1e9)
+    ap.add_argument("--chunk", type=int, default=1 << 27)
+    ap.add_argument("--cpu-sample", type=int, default=1_000_000)
+    args = ap.parse_args()
+    rank = _env_int("RANK", 0)
+    world = _env_int("WORLD_SIZE", 1)
+    local_rank = _env_int("LOCAL_RANK", 0)
+    args.warmup = max(3, args.warmup)  # the timing rules ask for at least 3 warm-up steps
+    if args.impl == "reference":
+        run_reference(args, rank)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

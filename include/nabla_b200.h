@@ -75,8 +75,16 @@ typedef struct nt_tape {
 
 /* Option flags. */
 #define NT_FLAG_NO_LOOP 0x1      /* emit straight-line code even when the tape has a step loop */
-#define NT_FLAG_GLOBAL_CKPT 0x2  /* keep step checkpoints in global memory instead of shared memory */
+#define NT_FLAG_SHARED_CKPT 0x2  /* keep step checkpoints in shared memory instead of (L2-resident)
+                                    global memory */
 #define NT_FLAG_NO_DISK_CACHE 0x4
+#define NT_FLAG_F32_FAST 0x8     /* fp32: exp/log and Box-Muller in single precision.  By default
+                                    they are evaluated in fp64 and narrowed on store, the reference's
+                                    fp32 semantics (ScalarReplay.java:37-51) */
+#define NT_FLAG_NO_FMAD 0x10     /* no multiply-add contraction (every product rounded) */
+#define NT_FLAG_ACC_REGS 0x20    /* keep the per-thread accumulators in registers, not shared memory */
+#define NT_FLAG_RECOMPUTE_ALL 0x40 /* reverse sweep recomputes every loop value from the step
+                                      checkpoints (no per-thread value tape in global memory) */
 
 /*
  * Compile options: AadOptions (AadOptions.java:42-156) plus the engine knobs a
@@ -92,6 +100,7 @@ typedef struct nt_options {
   int32_t min_blocks;  /* __launch_bounds__ minimum blocks per SM */
   int32_t max_regs;    /* register cap per thread */
   int32_t flags;       /* NT_FLAG_* */
+  int32_t fwd_unroll;  /* unroll of the forward step-unit loop */
 } nt_options;
 
 typedef struct nt_exec nt_exec;
@@ -117,6 +126,8 @@ typedef struct nt_exec_info {
   int32_t ckpt_slots;       /* checkpointed values per segment boundary */
   int32_t stored_per_unit;  /* values kept per unit for the reverse sweep */
   int32_t ckpt_global;      /* 1 when checkpoints live in global memory */
+  int32_t tape_slots;       /* values per loop unit written to the per-thread tape (0: recompute all) */
+  int32_t tape_mbytes;      /* device memory held by the value tape, MiB */
   double compile_seconds;   /* NVRTC + module load, 0 on a cache hit */
   double fwd_flops;         /* algorithmic flops per scenario, forward (weights in DESIGN) */
   double rev_flops;         /* algorithmic flops per scenario, reverse */
@@ -249,6 +260,12 @@ int nt_shard_range(uint64_t total_paths, uint64_t path_offset, int32_t nranks, i
  */
 int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
                     uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals);
+
+/* Measured vector-FMA peak of the device in TFLOP/s (FMA = 2 flops): the
+ * roofline denominator of the replay kernels, which run on the fp64 (or fp32)
+ * pipe, not the tensor cores.  fp64 != 0 measures DFMA, else FFMA.  No
+ * counterpart in the reference (it reports no roofline). */
+int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops);
 
 #ifdef __cplusplus
 }

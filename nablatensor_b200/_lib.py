@@ -29,8 +29,12 @@ NT_E_INTERNAL = -9
 NT_FLOAT32 = 0
 NT_FLOAT64 = 1
 NT_FLAG_NO_LOOP = 0x1
-NT_FLAG_GLOBAL_CKPT = 0x2
+NT_FLAG_SHARED_CKPT = 0x2
 NT_FLAG_NO_DISK_CACHE = 0x4
+NT_FLAG_F32_FAST = 0x8
+NT_FLAG_NO_FMAD = 0x10
+NT_FLAG_ACC_REGS = 0x20
+NT_FLAG_RECOMPUTE_ALL = 0x40
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f64p = ctypes.POINTER(ctypes.c_double)
@@ -46,14 +50,14 @@ class NtTape(ctypes.Structure):
 class NtOptions(ctypes.Structure):
     _fields_ = [("precision", ctypes.c_int32), ("adjoints", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("block", ctypes.c_int32), ("seg_units", ctypes.c_int32), ("min_blocks", ctypes.c_int32),
-                ("max_regs", ctypes.c_int32), ("flags", ctypes.c_int32)]
+                ("max_regs", ctypes.c_int32), ("flags", ctypes.c_int32), ("fwd_unroll", ctypes.c_int32)]
 
 
 class NtExecInfo(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in (
         "registers", "local_bytes", "static_smem", "dynamic_smem", "block", "blocks_per_sm", "grid", "sm_count",
         "channels", "loop_start", "loop_unit", "loop_units", "steps_per_unit", "seg_units", "segments",
-        "ckpt_slots", "stored_per_unit", "ckpt_global")] + [
+        "ckpt_slots", "stored_per_unit", "ckpt_global", "tape_slots", "tape_mbytes")] + [
         ("compile_seconds", ctypes.c_double), ("fwd_flops", ctypes.c_double), ("rev_flops", ctypes.c_double)]
 
     def as_dict(self) -> dict:
@@ -102,7 +106,15 @@ SIGNATURES = {
                         ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "nt_philox_words": ([ctypes.c_int32, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32,
                          ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32), _f64p], ctypes.c_int),
+    "nt_fma_peak": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
 }
+
+
+def fma_peak(device: int = 0, fp64: bool = True, iters: int = 4096) -> float:
+    """Measured vector-FMA peak in TFLOP/s (nt_fma_peak)."""
+    out = ctypes.c_double(0.0)
+    check(lib().nt_fma_peak(device, int(fp64), iters, ctypes.byref(out)))
+    return out.value
 
 
 def lib():
@@ -147,9 +159,9 @@ def tape_struct(tape):
 
 
 def options_struct(precision=NT_FLOAT64, adjoints=True, device=0, block=0, seg_units=0, min_blocks=0, max_regs=0,
-                   flags=0) -> NtOptions:
+                   flags=0, fwd_unroll=0) -> NtOptions:
     return NtOptions(int(precision), int(bool(adjoints)), int(device), int(block), int(seg_units), int(min_blocks),
-                     int(max_regs), int(flags))
+                     int(max_regs), int(flags), int(fwd_unroll))
 
 
 def emit_source(tape, target: int = 0, **opts) -> str:

@@ -147,18 +147,8 @@ int nt_exec_source(nt_exec* exec, char* buf, size_t cap, size_t* len) {
 int nt_emit_source(const nt_tape* tape, const nt_options* options, int32_t target, char* buf, size_t cap,
                    size_t* len) {
   return guarded([&] {
-    if (!options) nt::fail(NT_E_INVALID_ARG, "options are null");
-    if (target != 0 && target != 1) nt::fail(NT_E_INVALID_ARG, "target must be 0 (CUDA) or 1 (host)");
+    nt::EmitConfig cfg = nt::config_from(options, target);
     nt::Tape t = nt::ingest(tape);
-    nt::EmitConfig cfg;
-    cfg.f32 = options->precision == NT_FLOAT32;
-    cfg.adjoints = options->adjoints != 0;
-    cfg.no_loop = (options->flags & NT_FLAG_NO_LOOP) != 0;
-    cfg.global_ckpt = (options->flags & NT_FLAG_GLOBAL_CKPT) != 0;
-    cfg.block = options->block > 0 ? options->block : 128;
-    cfg.min_blocks = options->min_blocks;
-    cfg.seg_units = options->seg_units;
-    cfg.target = target;
     nt::Plan p = nt::plan_tape(t, cfg);
     copy_out(nt::emit(t, p, cfg), buf, cap, len);
   });
@@ -239,4 +229,12 @@ int nt_dist_detach(nt_exec* exec) {
 extern "C" int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
                                uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals) {
   return guarded([&] { nt::philox_words(device, path0, n_paths, seed, stream, pair0, n_pairs, out, normals); });
+}
+
+extern "C" int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops) {
+  return guarded([&] {
+    if (!tflops) nt::fail(NT_E_INVALID_ARG, "tflops is null");
+    if (iters <= 0) nt::fail(NT_E_INVALID_ARG, "iters must be positive");
+    *tflops = nt::fma_peak_tflops(device, fp64, iters);
+  });
 }

@@ -142,6 +142,21 @@ NT_FN void nt_normal_pair32(nt_key k, nt_u32 pair, float* c, float* s) {
   nt_bm32(w0, w1, c, s);
 }
 
+/* fp32 pair evaluated in fp64 and narrowed: the reference's fp32 semantics
+ * (each stored value is the double result rounded to float). */
+NT_FN void nt_normal_pair32w(nt_key k, nt_u32 pair, float* c, float* s) {
+  double cd, sd;
+  nt_normal_pair64(k, pair, &cd, &sd);
+  *c = (float)cd;
+  *s = (float)sd;
+}
+
+NT_FN float nt_normal32w(nt_key k, nt_u32 ordinal) {
+  float c, s;
+  nt_normal_pair32w(k, ordinal >> 1, &c, &s);
+  return (ordinal & 1u) ? s : c;
+}
+
 /* A single draw when its partner leg is not used in the same region. */
 NT_FN double nt_normal64(nt_key k, nt_u32 ordinal) {
   double c, s;

@@ -71,6 +71,12 @@ class Emitter {
   Out o_;
 
   std::string R(const char* f64, const char* f32) const { return cfg_.f32 ? f32 : f64; }
+  std::string rng_pair() const {
+    return cfg_.f32 ? (cfg_.wide32 ? "nt_normal_pair32w(" : "nt_normal_pair32(") : "nt_normal_pair64(";
+  }
+  std::string rng_single() const {
+    return cfg_.f32 ? (cfg_.wide32 ? "nt_normal32w(" : "nt_normal32(") : "nt_normal64(";
+  }
   int32_t channels() const { return t_.n_out() * (2 + t_.n_in()); }
   bool in_loop(int32_t x) const { return lp_.in(x); }
 
@@ -112,8 +118,8 @@ std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B
     case NT_MUL: return A + " * " + B;
     case NT_DIV: return A + " / " + B;
     case NT_NEG: return "-" + A;
-    case NT_EXP: return R("exp(", "expf(") + A + ")";
-    case NT_LOG: return R("log(", "logf(") + A + ")";
+    case NT_EXP: return cfg_.wide32 ? "((float)exp((double)" + A + "))" : R("exp(", "expf(") + A + ")";
+    case NT_LOG: return cfg_.wide32 ? "((float)log((double)" + A + "))" : R("log(", "logf(") + A + ")";
     case NT_SQRT: return R("sqrt(", "sqrtf(") + A + ")";
     case NT_ABS: return R("fabs(", "fabsf(") + A + ")";
     case NT_MAX: return R("nt_max64(", "nt_max32(") + A + ", " + B + ")";
@@ -191,11 +197,11 @@ void Emitter::emit_straight_forward(int32_t lo, int32_t hi) {
       const std::string key = "key" + std::to_string(t_.b[i]);
       if (even >= 0 && odd >= 0) {
         o_.line("real v" + std::to_string(even) + ", v" + std::to_string(odd) + ";");
-        o_.line(R("nt_normal_pair64(", "nt_normal_pair32(") + key + ", " + std::to_string(t_.a[i] >> 1) +
+        o_.line(rng_pair() + key + ", " + std::to_string(t_.a[i] >> 1) +
                 "u, &v" + std::to_string(even) + ", &v" + std::to_string(odd) + ");");
         done[even] = done[odd] = true;
       } else {
-        o_.line("const real " + vi + " = " + R("nt_normal64(", "nt_normal32(") + key + ", " +
+        o_.line("const real " + vi + " = " + rng_single() + key + ", " +
                 std::to_string(t_.a[i]) + "u);");
       }
       continue;
@@ -258,6 +264,11 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     if (recompute && !lp_.recompute[j]) continue;
     if (emitted[j]) continue;
     const BodyNode& bn = lp_.body[j];
+    if (recompute && lp_.tape_slot[j] >= 0) {
+      o_.line(name(j) + " = NT_TAPE(" + unit + ", " + std::to_string(lp_.tape_slot[j]) + ");");
+      emitted[j] = 1;
+      continue;
+    }
     const std::string key = "key" + std::to_string(bn.stream);
     if (bn.op == NT_RANDN) {
       auto it = partner.find(j);
@@ -265,11 +276,11 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
         const int32_t k = it->second;
         const int32_t ev = (bn.draw_base & 1) ? k : j, od = (bn.draw_base & 1) ? j : k;
         const int32_t pb = lp_.body[ev].draw_base >> 1, ps = bn.draw_stride >> 1;
-        o_.line(R("nt_normal_pair64(", "nt_normal_pair32(") + key + ", (nt_u32)(" + std::to_string(pb) + " + " +
+        o_.line(rng_pair() + key + ", (nt_u32)(" + std::to_string(pb) + " + " +
                 unit + " * " + std::to_string(ps) + "), &" + name(ev) + ", &" + name(od) + ");");
         emitted[ev] = emitted[od] = 1;
       } else {
-        o_.line(name(j) + " = " + R("nt_normal64(", "nt_normal32(") + key + ", (nt_u32)(" +
+        o_.line(name(j) + " = " + rng_single() + key + ", (nt_u32)(" +
                 std::to_string(bn.draw_base) + " + " + unit + " * " + std::to_string(bn.draw_stride) + "));");
         emitted[j] = 1;
       }
@@ -395,6 +406,7 @@ void Emitter::emit_reverse_for_output(int o) {
 void Emitter::acc_line(int32_t k, const std::string& x) {
   const std::string K = std::to_string(k);
   if (cfg_.target == 1) o_.line("nt_acc[" + K + "] += " + x + ";");
+  else if (cfg_.acc_smem) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
   else o_.line("nt_two_sum(&nt_acc[" + K + "], &nt_cmp[" + K + "], " + x + ");");
 }
 
@@ -422,13 +434,16 @@ void Emitter::emit_scenario() {
     o_.open("for (int s = 0; s < " + std::to_string(K) + "; ++s) {");
     for (int32_t c = 0; c < nck; ++c)
       o_.line("NT_CK(s * " + std::to_string(nck) + " + " + std::to_string(c) + ") = cv" + std::to_string(lp_.ckpt[c]) + ";");
-    if (cfg_.target == 0) o_.line("#pragma unroll 1");
+    if (cfg_.target == 0) o_.line("#pragma unroll " + std::to_string(std::max(1, cfg_.fwd_unroll)));
     o_.open("for (int g = 0; g < " + std::to_string(G) + "; ++g) {");
     o_.line("const int u = s * " + std::to_string(G) + " + g;");
     std::string decl;
     for (int32_t j = 0; j < L; ++j) decl += (j ? ", f" : "real f") + std::to_string(j);
     o_.line(decl + ";");
     emit_body_forward("f", "u", false, 0);
+    for (int32_t j = 0; j < L; ++j)
+      if (lp_.tape_slot[j] >= 0)
+        o_.line("NT_TAPE(u, " + std::to_string(lp_.tape_slot[j]) + ") = f" + std::to_string(j) + ";");
     for (int32_t k : lp_.carries) o_.line("cv" + std::to_string(k) + " = f" + std::to_string(k) + ";");
     for (int32_t j : lp_.exits)
       if (!lp_.is_carry[j]) o_.line("xv" + std::to_string(j) + " = f" + std::to_string(j) + ";");
@@ -457,8 +472,11 @@ std::string Emitter::run() {
   o_.line("#include \"nt_device_rt.cuh\"");
   o_.line(std::string("typedef ") + (cfg_.f32 ? "float" : "double") + " real;");
   o_.line("#define NT_CH " + std::to_string(channels()));
+  const int32_t ntape = lp_.present ? lp_.n_tape : 0;
+  o_.line("#define NT_NTAPE " + std::to_string(std::max(1, ntape)));
   if (host) {
     o_.line("#define NT_CK(slot) nt_ckbuf[(slot)]");
+    o_.line("#define NT_TAPE(u, slot) nt_tapebuf[(nt_u64)(u) * NT_NTAPE + (slot)]");
     o_.open("extern \"C\" void nt_host_replay(const double* inputs, uint64_t n_paths, uint64_t path_offset, uint64_t seed, double* sums) {");
     for (int32_t j = 0; j < t_.n_in(); ++j)
       o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
@@ -466,11 +484,14 @@ std::string Emitter::run() {
     o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = 0.0;");
     o_.line("real nt_ckbuf[" + std::to_string(std::max(1, nck_total)) + "];");
     o_.line("(void)nt_ckbuf;");
+    o_.line("real* nt_tapebuf = new real[" + std::to_string(std::max(1, (lp_.present ? lp_.N : 1) * std::max(1, ntape))) + "];");
+    o_.line("(void)nt_tapebuf;");
     o_.open("for (nt_u64 p = 0; p < n_paths; ++p) {");
     o_.line("const nt_u64 path = p + path_offset;");
     emit_scenario();
     o_.close();
     o_.line("for (int c = 0; c < NT_CH; ++c) sums[c] = nt_acc[c];");
+    o_.line("delete[] nt_tapebuf;");
     o_.close();
     return o_.s;
   }
@@ -480,28 +501,47 @@ std::string Emitter::run() {
   } else {
     o_.line("#define NT_CK(slot) nt_ck[(slot) * NT_BLOCK + threadIdx.x]");
   }
+  // Per-thread value tape, unit-major so each warp's store or load of one
+  // slot is 32 consecutive values (one coalesced 256-byte transaction in fp64).
+  o_.line("#define NT_TAPE(u, slot) nt_tape[((nt_u64)(u) * NT_NTAPE + (slot)) * nt_gthreads + nt_gtid]");
   std::string bounds = "__launch_bounds__(NT_BLOCK" + (cfg_.min_blocks > 0 ? ", " + std::to_string(cfg_.min_blocks) : std::string()) + ")";
   o_.line("extern \"C\" __global__ void " + bounds + " nt_replay_kernel(");
   o_.line("    const double* __restrict__ inputs, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
   o_.line("    double* __restrict__ partials, unsigned int* __restrict__ ticket, double* __restrict__ out,");
-  o_.line("    int accumulate, real* __restrict__ nt_gck) {");
+  o_.line("    int accumulate, real* __restrict__ nt_gck, real* __restrict__ nt_tape) {");
   ++o_.ind;
   if (!cfg_.global_ckpt) o_.line("extern __shared__ real nt_ck[];");
   o_.line("__shared__ double nt_red[NT_CH * (NT_BLOCK / 32)];");
   o_.line("const nt_u64 nt_gtid = (nt_u64)blockIdx.x * NT_BLOCK + threadIdx.x;");
   o_.line("const nt_u64 nt_gthreads = (nt_u64)gridDim.x * NT_BLOCK;");
-  o_.line("(void)nt_gck; (void)nt_gthreads;");
+  o_.line("(void)nt_gck; (void)nt_gthreads; (void)nt_tape;");
   for (int32_t j = 0; j < t_.n_in(); ++j)
     o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
-  o_.line("double nt_acc[NT_CH], nt_cmp[NT_CH];");
-  o_.line("#pragma unroll");
-  o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
+  if (cfg_.acc_smem) {
+    // Compensated accumulators live in shared memory (one column per thread):
+    // they are touched once per scenario, so registers are better spent on
+    // the segment buffer and occupancy.
+    o_.line("__shared__ double nt_accs[2 * NT_CH * NT_BLOCK];");
+    o_.line("#define NT_ACC(k) nt_accs[(2 * (k)) * NT_BLOCK + threadIdx.x]");
+    o_.line("#define NT_CMP(k) nt_accs[(2 * (k) + 1) * NT_BLOCK + threadIdx.x]");
+    o_.line("for (int c = 0; c < NT_CH; ++c) { NT_ACC(c) = 0.0; NT_CMP(c) = 0.0; }");
+  } else {
+    o_.line("double nt_acc[NT_CH], nt_cmp[NT_CH];");
+    o_.line("#pragma unroll");
+    o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
+  }
   o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
   o_.line("const nt_u64 path = p + path_offset;");
   emit_scenario();
   o_.close();
-  o_.line("#pragma unroll");
-  o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] += nt_cmp[c];");
+  if (cfg_.acc_smem) {
+    o_.line("double nt_acc[NT_CH];");
+    o_.line("#pragma unroll");
+    o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = NT_ACC(c) + NT_CMP(c);");
+  } else {
+    o_.line("#pragma unroll");
+    o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] += nt_cmp[c];");
+  }
   o_.line("nt_grid_reduce(nt_acc, NT_CH, nt_red, partials, ticket, out, accumulate);");
   o_.close();
   return o_.s;

@@ -157,19 +157,9 @@ void cuda_check(cudaError_t e, const char* what) {
 // ---- compile / set-up ---------------------------------------------------------
 
 Exec* Exec::create(const nt_tape* tape, const nt_options* opt) {
-  if (!opt) fail(NT_E_INVALID_ARG, "options are null");
-  if (opt->precision != NT_FLOAT32 && opt->precision != NT_FLOAT64) fail(NT_E_INVALID_ARG, "bad precision");
   std::unique_ptr<Exec> x(new Exec());
+  x->cfg = config_from(opt, 0);
   x->tape = ingest(tape);
-  x->cfg.f32 = opt->precision == NT_FLOAT32;
-  x->cfg.adjoints = opt->adjoints != 0;
-  x->cfg.no_loop = (opt->flags & NT_FLAG_NO_LOOP) != 0;
-  x->cfg.global_ckpt = (opt->flags & NT_FLAG_GLOBAL_CKPT) != 0;
-  x->cfg.block = opt->block > 0 ? opt->block : 128;
-  if (x->cfg.block % 32 != 0 || x->cfg.block > 1024) fail(NT_E_INVALID_ARG, "block must be a multiple of 32, <= 1024");
-  x->cfg.min_blocks = opt->min_blocks;
-  x->cfg.seg_units = opt->seg_units;
-  x->cfg.target = 0;
   x->device = opt->device;
   x->use_disk_cache = (opt->flags & NT_FLAG_NO_DISK_CACHE) == 0;
   x->plan = plan_tape(x->tape, x->cfg);
@@ -199,12 +189,13 @@ void Exec::load(int max_regs) {
   sm_count = prop.multiProcessorCount;
   (void)max_regs;
   double secs = 0.0;
-  std::vector<char> cubin = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs);
+  std::vector<char> cubin = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs, cfg.fmad);
   const auto t0 = std::chrono::steady_clock::now();
   Driver& d = driver();
   cu_check(d.moduleLoadData(&module, cubin.data()), "cuModuleLoadData");
   cu_check(d.moduleGetFunction(&function, module, "nt_replay_kernel"), "cuModuleGetFunction");
-  if (dyn_smem > 48 * 1024)
+  // Static + dynamic shared memory above 48 KB needs the opt-in attribute.
+  if (dyn_smem > 0)
     cu_check(d.funcSetAttribute(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_smem),
              "cuFuncSetAttribute");
   int regs = 0, local = 0, ssm = 0;
@@ -229,6 +220,13 @@ void Exec::load(int max_regs) {
     const size_t bytes = (size_t)ckpt_values(plan) * grid * cfg.block * (cfg.f32 ? 4 : 8);
     cuda_check(cudaMalloc(&d_gck, bytes), "cudaMalloc checkpoints");
   }
+  // The value tape: one slab per resident thread (indexed by the launched
+  // grid, never larger than the persistent grid sized here).
+  size_t tape_bytes = 0;
+  if (plan.loop.present && plan.loop.n_tape > 0) {
+    tape_bytes = (size_t)plan.loop.N * plan.loop.n_tape * grid * cfg.block * (cfg.f32 ? 4 : 8);
+    cuda_check(cudaMalloc(&d_tape, tape_bytes), "cudaMalloc value tape");
+  }
   cuda_check(cudaMallocHost(&h_stage, sizeof(double) * (tape.n_in() + 2 * channels + 2)), "cudaMallocHost");
   compile_seconds = secs + std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   std::memset(&info, 0, sizeof info);
@@ -251,6 +249,8 @@ void Exec::load(int max_regs) {
   info.ckpt_slots = lp.present ? (int32_t)lp.ckpt.size() : 0;
   info.stored_per_unit = plan.stored_per_unit;
   info.ckpt_global = cfg.global_ckpt ? 1 : 0;
+  info.tape_slots = lp.present ? lp.n_tape : 0;
+  info.tape_mbytes = (int32_t)(tape_bytes >> 20);
   info.compile_seconds = compile_seconds;
   info.fwd_flops = plan.fwd_flops;
   info.rev_flops = plan.rev_flops;
@@ -270,6 +270,7 @@ Exec::~Exec() {
   cudaFree(d_acc);
   cudaFree(d_red);
   cudaFree(d_gck);
+  cudaFree(d_tape);
   if (h_stage) cudaFreeHost(h_stage);
   if (stream) cudaStreamDestroy(stream);
   if (module) driver().moduleUnload(module);
@@ -291,8 +292,9 @@ void Exec::launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, i
   const uint64_t need = (paths + cfg.block - 1) / cfg.block;
   const unsigned g = (unsigned)std::min<uint64_t>(need, (uint64_t)grid);
   void* gck = d_gck;
+  void* tp = d_tape;
   unsigned long long n = paths, off = offset, sd = seed;
-  void* args[] = {&d_inputs, &n, &off, &sd, &d_partials, &d_ticket, &out, &accumulate, &gck};
+  void* args[] = {&d_inputs, &n, &off, &sd, &d_partials, &d_ticket, &out, &accumulate, &gck, &tp};
   cu_check(driver().launchKernel(function, g, 1, 1, (unsigned)cfg.block, 1, 1, (unsigned)dyn_smem,
                                  (CUstream)stream, args, nullptr),
            "cuLaunchKernel");

@@ -36,6 +36,7 @@ struct Exec {
   double* d_acc = nullptr;
   double* d_red = nullptr;
   void* d_gck = nullptr;
+  void* d_tape = nullptr;
   double* h_stage = nullptr;  // pinned: inputs, then sums
   std::vector<double> inputs;
   bool dirty = true;

@@ -77,6 +77,8 @@ struct Loop {
   std::vector<int32_t> ckpt;        // carries saved at each segment boundary
   std::vector<uint8_t> stored;      // per offset: value kept for the reverse sweep
   std::vector<uint8_t> recompute;   // per offset: recomputed from the segment checkpoint
+  std::vector<int32_t> tape_slot;   // per offset: slot in the per-thread value tape, or -1
+  int32_t n_tape = 0;               // taped values per unit
   int32_t G = 0;                    // units per segment
   int32_t K = 0;                    // segments (N = K * G)
   int32_t end() const { return B + N * L; }
@@ -97,11 +99,19 @@ struct EmitConfig {
   bool adjoints = true;
   bool no_loop = false;
   bool global_ckpt = false;
+  bool wide32 = false;     // fp32: transcendentals + Box-Muller in fp64, narrowed
+  bool fmad = true;        // allow multiply-add contraction
+  bool acc_smem = true;    // compensated accumulators in shared memory
+  bool tape = true;        // expensive loop values go to a per-thread tape instead of being recomputed
+  int32_t fwd_unroll = 1;  // unroll of the forward unit loop
   int32_t block = 128;
   int32_t min_blocks = 0;
   int32_t seg_units = 0;   // 0 = automatic
   int32_t target = 0;      // 0 CUDA, 1 host C++
 };
+
+// Emitter configuration from the C ABI options (validates them).
+EmitConfig config_from(const nt_options* opt, int32_t target);
 
 // Finds the step loop and the checkpoint / recompute sets.
 Plan plan_tape(const Tape& t, const EmitConfig& cfg);
@@ -118,12 +128,15 @@ extern const char* kDeviceRuntimeSource;  // nt_device_rt.cuh, embedded at build
 // (nt_flops.cpp), used for the algorithmic flop count of a tape.
 extern const double kFlopWeights[4];
 
+// Vector-FMA peak (TFLOP/s) measured with independent FMA chains.
+double fma_peak_tflops(int32_t device, int32_t fp64, int32_t iters);
+
 // Runs the device Philox/Box-Muller for the known-answer interface.
 void philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
                   uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals);
 
 // NVRTC: compile to an sm_100a cubin (cached in memory and on disk).
 std::vector<char> nvrtc_compile(const std::string& source, const std::string& arch, bool use_disk_cache,
-                                double* seconds);
+                                double* seconds, bool fmad = true);
 
 }  // namespace nt

@@ -65,3 +65,69 @@ void philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t see
 }
 
 }  // namespace nt
+
+// ---- fp64 / fp32 vector-FMA peak ------------------------------------------------
+//
+// The roofline denominator for the replay kernels: MEASURED_PEAKS.json holds
+// HBM and bf16 tensor figures only.  Each thread runs `chains` independent
+// FMA chains (enough to cover the pipe latency) for `iters` iterations; the
+// result is stored so nothing is optimised away.
+
+namespace {
+
+template <typename T>
+__global__ void __launch_bounds__(256) fma_peak_kernel(T* out, int iters, T a, T b) {
+  T x0 = (T)threadIdx.x, x1 = x0 + (T)1, x2 = x0 + (T)2, x3 = x0 + (T)3;
+  T x4 = x0 + (T)4, x5 = x0 + (T)5, x6 = x0 + (T)6, x7 = x0 + (T)7;
+  for (int i = 0; i < iters; ++i) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      x0 = fma(x0, a, b); x1 = fma(x1, a, b); x2 = fma(x2, a, b); x3 = fma(x3, a, b);
+      x4 = fma(x4, a, b); x5 = fma(x5, a, b); x6 = fma(x6, a, b); x7 = fma(x7, a, b);
+    }
+  }
+  out[(size_t)blockIdx.x * blockDim.x + threadIdx.x] = x0 + x1 + x2 + x3 + x4 + x5 + x6 + x7;
+}
+
+}  // namespace
+
+namespace nt {
+
+double fma_peak_tflops(int32_t device, int32_t fp64, int32_t iters) {
+  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop;
+  cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  int per_sm = 0;
+  if (fp64)
+    cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fma_peak_kernel<double>, 256, 0), "occupancy");
+  else
+    cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fma_peak_kernel<float>, 256, 0), "occupancy");
+  const int blocks = prop.multiProcessorCount * per_sm;
+  void* out = nullptr;
+  cudaStream_t s = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaMalloc(&out, (size_t)blocks * 256 * 8), "cudaMalloc");
+  cuda_check(cudaEventCreate(&e0), "cudaEventCreate");
+  cuda_check(cudaEventCreate(&e1), "cudaEventCreate");
+  float best_ms = 1e30f;
+  for (int rep = 0; rep < 4; ++rep) {
+    cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
+    if (fp64) fma_peak_kernel<double><<<blocks, 256, 0, s>>>((double*)out, iters, 0.999999, 1e-7);
+    else fma_peak_kernel<float><<<blocks, 256, 0, s>>>((float*)out, iters, 0.999999f, 1e-7f);
+    cuda_check(cudaGetLastError(), "fma_peak_kernel");
+    cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
+    cuda_check(cudaEventSynchronize(e1), "fma_peak_kernel");
+    float ms = 0;
+    cuda_check(cudaEventElapsedTime(&ms, e0, e1), "cudaEventElapsedTime");
+    if (rep > 0 && ms < best_ms) best_ms = ms;  // first launch is warm-up
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(out);
+  cudaStreamDestroy(s);
+  const double flops = 2.0 * 8 * 16 * (double)iters * blocks * 256;
+  return flops / (best_ms * 1e-3) / 1e12;
+}
+
+}  // namespace nt

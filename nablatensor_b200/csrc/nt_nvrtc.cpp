@@ -60,13 +60,13 @@ void check(nvrtcResult r, const char* what) {
 }  // namespace
 
 std::vector<char> nvrtc_compile(const std::string& source, const std::string& arch, bool use_disk_cache,
-                                double* seconds) {
+                                double* seconds, bool fmad) {
   int major = 0, minor = 0;
   nvrtcVersion(&major, &minor);
   std::vector<std::string> opts = {
       "--gpu-architecture=" + arch,
       "--std=c++17",
-      "--fmad=true",
+      fmad ? "--fmad=true" : "--fmad=false",
       "-default-device",
       "--extra-device-vectorization",
       "-lineinfo",

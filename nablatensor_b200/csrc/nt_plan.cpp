@@ -271,6 +271,31 @@ struct Weights {
 
 }  // namespace
 
+EmitConfig config_from(const nt_options* opt, int32_t target) {
+  if (!opt) fail(NT_E_INVALID_ARG, "options are null");
+  if (opt->precision != NT_FLOAT32 && opt->precision != NT_FLOAT64) fail(NT_E_INVALID_ARG, "bad precision");
+  if (target != 0 && target != 1) fail(NT_E_INVALID_ARG, "target must be 0 (CUDA) or 1 (host)");
+  EmitConfig cfg;
+  cfg.f32 = opt->precision == NT_FLOAT32;
+  cfg.adjoints = opt->adjoints != 0;
+  cfg.no_loop = (opt->flags & NT_FLAG_NO_LOOP) != 0;
+  cfg.global_ckpt = (opt->flags & NT_FLAG_SHARED_CKPT) == 0;
+  cfg.wide32 = cfg.f32 && (opt->flags & NT_FLAG_F32_FAST) == 0;
+  cfg.fmad = (opt->flags & NT_FLAG_NO_FMAD) == 0;
+  cfg.block = opt->block > 0 ? opt->block : 128;
+  if (cfg.block % 32 != 0 || cfg.block > 1024) fail(NT_E_INVALID_ARG, "block must be a multiple of 32, <= 1024");
+  if (opt->min_blocks < 0 || opt->min_blocks > 32) fail(NT_E_INVALID_ARG, "min_blocks must be in [0, 32]");
+  if (opt->seg_units < 0) fail(NT_E_INVALID_ARG, "seg_units must be >= 0");
+  cfg.min_blocks = opt->min_blocks;
+  cfg.seg_units = opt->seg_units;
+  cfg.target = target;
+  if (opt->fwd_unroll < 0 || opt->fwd_unroll > 16) fail(NT_E_INVALID_ARG, "fwd_unroll must be in [0, 16]");
+  cfg.fwd_unroll = opt->fwd_unroll > 0 ? opt->fwd_unroll : 1;
+  cfg.acc_smem = (opt->flags & NT_FLAG_ACC_REGS) == 0;
+  cfg.tape = (opt->flags & NT_FLAG_RECOMPUTE_ALL) == 0;
+  return cfg;
+}
+
 int32_t ckpt_values(const Plan& p) {
   return p.loop.present ? p.loop.K * (int32_t)p.loop.ckpt.size() : 0;
 }
@@ -351,13 +376,21 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
         else if (r.kind == REF_CARRY) { lp.stored[r.idx] = 1; carry_read[r.idx] = 1; }
       }
     }
-    // Recompute closure: nodes needed to regenerate the stored values.
+    // Recompute closure: nodes needed to regenerate the stored values.  In
+    // tape mode an expensive node (a draw, exp, log, sqrt or division) is a
+    // leaf: the forward sweep writes its value to the thread's tape and the
+    // reverse sweep reads it back instead of recomputing its inputs.
+    auto expensive = [&](int op) {
+      return op == NT_RANDN || op == NT_RANDU || op == NT_EXP || op == NT_LOG || op == NT_SQRT || op == NT_DIV;
+    };
     std::vector<uint8_t> need(lp.stored);
+    lp.tape_slot.assign(L, -1);
     for (bool changed = true; changed;) {
       changed = false;
       for (int32_t j = L - 1; j >= 0; --j) {
         if (!need[j]) continue;
         const BodyNode& bn = lp.body[j];
+        if (cfg.tape && expensive(bn.op)) continue;  // a tape leaf
         for (int w = 0; w < nargs(bn.op); ++w) {
           const Ref& r = w == 0 ? bn.ra : bn.rb;
           if ((r.kind == REF_SAME || r.kind == REF_CARRY) && !need[r.idx]) { need[r.idx] = 1; changed = true; }
@@ -366,6 +399,10 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
       }
     }
     lp.recompute = need;
+    lp.n_tape = 0;
+    if (cfg.tape)
+      for (int32_t j = 0; j < L; ++j)
+        if (need[j] && expensive(lp.body[j].op)) lp.tape_slot[j] = lp.n_tape++;
     lp.ckpt.clear();
     for (int32_t k : lp.carries)
       if (carry_read[k]) lp.ckpt.push_back(k);

@@ -163,7 +163,11 @@ class AadExecutable:
         raise NotImplementedError
 
 
-_ENGINE_KEYS = {"block": "block", "segUnits": "seg_units", "minBlocks": "min_blocks", "maxRegs": "max_regs"}
+_ENGINE_KEYS = {"block": "block", "segUnits": "seg_units", "minBlocks": "min_blocks", "maxRegs": "max_regs",
+                "fwdUnroll": "fwd_unroll"}
+_ENGINE_FLAGS = {"noLoop": _lib.NT_FLAG_NO_LOOP, "sharedCheckpoints": _lib.NT_FLAG_SHARED_CKPT,
+                 "fp32Fast": _lib.NT_FLAG_F32_FAST, "noFmad": _lib.NT_FLAG_NO_FMAD,
+                 "accRegisters": _lib.NT_FLAG_ACC_REGS, "recomputeAll": _lib.NT_FLAG_RECOMPUTE_ALL}
 
 
 class B200AadExecutable(AadExecutable):
@@ -177,10 +181,10 @@ class B200AadExecutable(AadExecutable):
         for k, v in options.engine_options_for("cuda").items():
             if k in _ENGINE_KEYS:
                 knobs[_ENGINE_KEYS[k]] = int(v)
-            elif k == "noLoop" and str(v).lower() in ("1", "true", "on"):
-                flags |= _lib.NT_FLAG_NO_LOOP
-            elif k == "globalCheckpoints" and str(v).lower() in ("1", "true", "on"):
-                flags |= _lib.NT_FLAG_GLOBAL_CKPT
+            elif k in _ENGINE_FLAGS and str(v).lower() in ("1", "true", "on"):
+                flags |= _ENGINE_FLAGS[k]
+            elif k not in _ENGINE_FLAGS:
+                raise ValueError(f"unknown cuda engine option: {k}")
         s, keep = _lib.tape_struct(tape)
         o = _lib.options_struct(precision=int(options.precision), adjoints=options.adjoints, device=device,
                                 flags=flags, **knobs)
