@@ -277,7 +277,15 @@ def main():
     ap.add_argument("--paths", type=float, default=1e9)
     ap.add_argument("--chunk", type=int, default=1 << 27)
     ap.add_argument("--cpu-sample", type=int, default=1_000_000)
+    ap.add_argument("--math-probes", action="store_true",
+                    help="launch each math-probe kernel once (for ncu per-call instruction/flop counts)")
     args = ap.parse_args()
+    if args.math_probes:
+        from nablatensor_b200 import _lib
+        for which, name in _lib.MATH_PROBES.items():
+            _lib.math_probe(0, which, 64)
+            print(f"probe {which}: {name}", flush=True)
+        return
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
     local_rank = _env_int("LOCAL_RANK", 0)

@@ -267,6 +267,13 @@ int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t s
  * counterpart in the reference (it reports no roofline). */
 int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops);
 
+/* Launches one math-probe kernel (148*4 blocks of 256 threads, `iters` calls
+ * each) for instruction / flop counting under ncu: which = 0 empty loop,
+ * 1 library exp, 2 library log, 3 library sincos, 4 library sqrt, 5 the
+ * replay's exp, 6 its -2 ln(u1), 7 its sincos(2 pi u2), 8 library exp on a
+ * wide range.  No counterpart in the reference. */
+int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
+
 #ifdef __cplusplus
 }
 #endif

@@ -107,7 +107,17 @@ SIGNATURES = {
     "nt_philox_words": ([ctypes.c_int32, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32,
                          ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32), _f64p], ctypes.c_int),
     "nt_fma_peak": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
+    "nt_math_probe": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
 }
+
+MATH_PROBES = {0: "loop", 1: "exp(lib, |x|<=1/8)", 2: "log(lib)", 3: "sincos(lib)", 4: "sqrt(lib)",
+               5: "exp(replay)", 6: "-2ln(u1)(replay)", 7: "sincos(2pi u2)(replay)", 8: "exp(lib, |x|<=4)"}
+
+
+def math_probe(device: int, which: int, iters: int) -> float:
+    out = ctypes.c_double(0.0)
+    check(lib().nt_math_probe(device, which, iters, ctypes.byref(out)))
+    return out.value
 
 
 def fma_peak(device: int = 0, fp64: bool = True, iters: int = 4096) -> float:

@@ -231,6 +231,14 @@ extern "C" int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths,
   return guarded([&] { nt::philox_words(device, path0, n_paths, seed, stream, pair0, n_pairs, out, normals); });
 }
 
+extern "C" int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum) {
+  return guarded([&] {
+    if (which < 0 || which > 8) nt::fail(NT_E_INVALID_ARG, "which must be in [0, 8]");
+    if (iters <= 0) nt::fail(NT_E_INVALID_ARG, "iters must be positive");
+    nt::math_probe(device, which, iters, checksum);
+  });
+}
+
 extern "C" int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops) {
   return guarded([&] {
     if (!tflops) nt::fail(NT_E_INVALID_ARG, "tflops is null");

@@ -92,21 +92,190 @@ NT_FN void nt_normal_words(nt_key k, nt_u32 pair, nt_u32* w0, nt_u32* w1) {
   nt_philox(k.lo, k.hi ^ pair, w0, w1);
 }
 
-/* fp64 Box-Muller of one block: cosine leg (even ordinal) and sine leg (odd). */
+/* ---- fp64 elementary functions for the replay kernels ---------------------
+ *
+ * Written from the textbook methods (Cody and Waite, "Software Manual for the
+ * Elementary Functions", 1980: argument reduction with a constant split in
+ * two parts; Taylor / atanh series on the reduced range).  They exploit what
+ * the replay knows about its arguments -- the Box-Muller inputs are 32-bit
+ * generator words, GBM log-returns are small -- so they carry none of the
+ * special-case handling a general-purpose routine needs.  Accuracy (checked
+ * by the tests against libm and the device library): within 2 ulp.
+ */
+
+NT_FN int nt_hiword(double x) {
+#ifdef NT_HOST
+  long long b;
+  memcpy(&b, &x, sizeof b);
+  return (int)(b >> 32);
+#else
+  return __double2hiint(x);
+#endif
+}
+
+NT_FN unsigned nt_loword(double x) {
+#ifdef NT_HOST
+  long long b;
+  memcpy(&b, &x, sizeof b);
+  return (unsigned)b;
+#else
+  return (unsigned)__double2loint(x);
+#endif
+}
+
+NT_FN double nt_from_words(int hi, unsigned lo) {
+#ifdef NT_HOST
+  long long b = ((long long)hi << 32) | (long long)lo;
+  double x;
+  memcpy(&x, &b, sizeof x);
+  return x;
+#else
+  return __hiloint2double(hi, (int)lo);
+#endif
+}
+
+/* -2 ln(u1), u1 = (w0 + 0.5) 2^-32 (exact, in (2^-33, 1)).
+ * u1 = m 2^k with m in [sqrt(1/2), sqrt(2)); ln m = 2 atanh(s), s = (m-1)/(m+1),
+ * |s| < 0.1716, summed to s^23 (truncation < 2^-60 relative); ln2 is split so
+ * that k ln2_hi is exact.  1/(m+1) is a single-precision seed refined by two
+ * Newton steps, and s by one residual correction. */
+NT_FN double nt_neg2log_u1(nt_u32 w0) {
+  const double u = ((double)w0 + 0.5) * NT_UINT_SCALE;
+  const int hi = nt_hiword(u);
+  int k = ((hi >> 20) & 0x7ff) - 1023;
+  int mhi = (hi & 0x000fffff) | 0x3ff00000; /* m in [1, 2) */
+  if (mhi >= 0x3ff6a09f) {                   /* m >= sqrt(2): use m / 2 */
+    mhi -= 0x00100000;
+    k += 1;
+  }
+  const double m = nt_from_words(mhi, nt_loword(u));
+  const double f = m - 1.0; /* exact */
+  const double d = m + 1.0;
+#ifdef NT_HOST
+  double y = (double)(1.0f / (float)d);
+#else
+  float yf;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yf) : "f"((float)d));
+  double y = (double)yf;
+#endif
+  double e = fma(-d, y, 1.0);
+  y = fma(y, e, y);
+  e = fma(-d, y, 1.0);
+  y = fma(y, e, y);
+  double s = f * y;
+  s = fma(fma(-s, d, f), y, s);
+  const double z = s * s;
+  double p = 1.0 / 23.0;
+  p = fma(p, z, 1.0 / 21.0);
+  p = fma(p, z, 1.0 / 19.0);
+  p = fma(p, z, 1.0 / 17.0);
+  p = fma(p, z, 1.0 / 15.0);
+  p = fma(p, z, 1.0 / 13.0);
+  p = fma(p, z, 1.0 / 11.0);
+  p = fma(p, z, 1.0 / 9.0);
+  p = fma(p, z, 1.0 / 7.0);
+  p = fma(p, z, 1.0 / 5.0);
+  p = fma(p, z, 1.0 / 3.0);
+  const double lnm = 2.0 * fma(s * z, p, s);
+  const double kd = (double)k;
+  const double ln_u = fma(kd, 0x1.62e42p-1 /* ln2 hi */, fma(kd, 0x1.fdf473de6af28p-22 /* ln2 lo */, lnm));
+  return -2.0 * ln_u;
+}
+
+/* sin and cos of the reference's angle fl(2 pi u2), u2 = (w1 + 0.5) 2^-32.
+ * theta = k pi/2 + x with pi/2 in two parts (the first product exact), then
+ * Taylor series on |x| <= pi/4 to x^17 (sin) and x^16 (cos). */
+NT_FN void nt_sincos_2pi_u2(nt_u32 w1, double* sn, double* cs) {
+  const double u2 = ((double)w1 + 0.5) * NT_UINT_SCALE;
+  const double th = NT_TWO_PI * u2;
+#ifdef NT_HOST
+  const int k = (int)nearbyint(th * 0.6366197723675814);
+#else
+  const int k = __double2int_rn(th * 0.6366197723675814);
+#endif
+  const double kd = (double)k;
+  double x = fma(-kd, 0x1.921fb54442d18p+0 /* pi/2 hi */, th);
+  x = fma(-kd, 0x1.1a62633145c07p-54 /* pi/2 lo */, x);
+  const double z = x * x;
+  double ps = 1.0 / 355687428096000.0;     /* 1/17! */
+  ps = fma(ps, z, -1.0 / 1307674368000.0); /* 1/15! */
+  ps = fma(ps, z, 1.0 / 6227020800.0);     /* 1/13! */
+  ps = fma(ps, z, -1.0 / 39916800.0);      /* 1/11! */
+  ps = fma(ps, z, 1.0 / 362880.0);         /* 1/9!  */
+  ps = fma(ps, z, -1.0 / 5040.0);          /* 1/7!  */
+  ps = fma(ps, z, 1.0 / 120.0);            /* 1/5!  */
+  ps = fma(ps, z, -1.0 / 6.0);             /* 1/3!  */
+  const double s = fma(x * z, ps, x);
+  double pc = 1.0 / 20922789888000.0;      /* 1/16! */
+  pc = fma(pc, z, -1.0 / 87178291200.0);   /* 1/14! */
+  pc = fma(pc, z, 1.0 / 479001600.0);      /* 1/12! */
+  pc = fma(pc, z, -1.0 / 3628800.0);       /* 1/10! */
+  pc = fma(pc, z, 1.0 / 40320.0);          /* 1/8!  */
+  pc = fma(pc, z, -1.0 / 720.0);           /* 1/6!  */
+  pc = fma(pc, z, 1.0 / 24.0);             /* 1/4!  */
+  pc = fma(pc, z, -0.5);                   /* 1/2!  */
+  const double c = fma(z, pc, 1.0);
+  const int q = k & 3;
+  double so = (q & 1) ? c : s;
+  double co = (q & 1) ? s : c;
+  if (q & 2) so = -so;
+  if ((q + 1) & 2) co = -co;
+  *sn = so;
+  *cs = co;
+}
+
+/* exp(x): |x| <= 1/8 (every GBM log-return) by its Taylor series to x^10
+ * (truncation < 2^-58 relative); otherwise the library exp. */
+NT_FN double nt_exp_small(double x) {
+  double p = 1.0 / 3628800.0;
+  p = fma(p, x, 1.0 / 362880.0);
+  p = fma(p, x, 1.0 / 40320.0);
+  p = fma(p, x, 1.0 / 5040.0);
+  p = fma(p, x, 1.0 / 720.0);
+  p = fma(p, x, 1.0 / 120.0);
+  p = fma(p, x, 1.0 / 24.0);
+  p = fma(p, x, 1.0 / 6.0);
+  p = fma(p, x, 0.5);
+  p = fma(p, x, 1.0);
+  return fma(p, x, 1.0);
+}
+
+NT_FN double nt_exp64(double x) {
+  if (fabs(x) <= 0.125) return nt_exp_small(x);
+  return exp(x);
+}
+
+/* EXP nodes of fp64 tapes: the dedicated routine on the device, libm in the
+ * host build (bit-for-bit with the oracle). */
+#ifdef NT_HOST
+#define NT_EXP64(x) exp(x)
+#else
+#define NT_EXP64(x) nt_exp64(x)
+#endif
+
+/* Box-Muller legs from the dedicated routines above. */
+NT_FN void nt_bm64_words(nt_u32 w0, nt_u32 w1, double* cos_leg, double* sin_leg) {
+  const double r = sqrt(nt_neg2log_u1(w0));
+  double s, c;
+  nt_sincos_2pi_u2(w1, &s, &c);
+  *cos_leg = r * c;
+  *sin_leg = r * s;
+}
+
+/* fp64 Box-Muller of one block: cosine leg (even ordinal) and sine leg (odd).
+ * The device uses the dedicated routines; the host build (the emitter's
+ * test target) uses libm exactly as the oracle does. */
 NT_FN void nt_bm64(nt_u32 w0, nt_u32 w1, double* cos_leg, double* sin_leg) {
+#ifdef NT_HOST
   double u1 = ((double)w0 + 0.5) * NT_UINT_SCALE;
   double u2 = ((double)w1 + 0.5) * NT_UINT_SCALE;
   double r = sqrt(-2.0 * log(u1));
   double a = NT_TWO_PI * u2;
-  double s, c;
-#ifdef NT_HOST
-  s = sin(a);
-  c = cos(a);
+  *cos_leg = r * cos(a);
+  *sin_leg = r * sin(a);
 #else
-  sincos(a, &s, &c);
+  nt_bm64_words(w0, w1, cos_leg, sin_leg);
 #endif
-  *cos_leg = r * c;
-  *sin_leg = r * s;
 }
 
 /* fp32 Box-Muller: the uint32 words are the fp64 generator's; u1 is rounded

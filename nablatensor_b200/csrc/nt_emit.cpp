@@ -118,7 +118,7 @@ std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B
     case NT_MUL: return A + " * " + B;
     case NT_DIV: return A + " / " + B;
     case NT_NEG: return "-" + A;
-    case NT_EXP: return cfg_.wide32 ? "((float)exp((double)" + A + "))" : R("exp(", "expf(") + A + ")";
+    case NT_EXP: return cfg_.wide32 ? "((float)NT_EXP64((double)" + A + "))" : R("NT_EXP64(", "expf(") + A + ")";
     case NT_LOG: return cfg_.wide32 ? "((float)log((double)" + A + "))" : R("log(", "logf(") + A + ")";
     case NT_SQRT: return R("sqrt(", "sqrtf(") + A + ")";
     case NT_ABS: return R("fabs(", "fabsf(") + A + ")";

@@ -128,6 +128,9 @@ extern const char* kDeviceRuntimeSource;  // nt_device_rt.cuh, embedded at build
 // (nt_flops.cpp), used for the algorithmic flop count of a tape.
 extern const double kFlopWeights[4];
 
+// Math probe launches (per-call counts under ncu).
+void math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
+
 // Vector-FMA peak (TFLOP/s) measured with independent FMA chains.
 double fma_peak_tflops(int32_t device, int32_t fp64, int32_t iters);
 

@@ -430,8 +430,9 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
       case NT_LOG: fwd += w.log; break;
       case NT_SQRT: fwd += w.sqrt; break;
       case NT_RANDN:
-        // one Box-Muller pair per two normals: log + sqrt + sincos + 6 flops
-        fwd += 0.5 * (w.log + w.sqrt + w.sincos + 6.0);
+        // one Box-Muller pair per two normals: log + sqrt + sincos, plus
+        // u1, u2 (2 adds, 2 multiplies), -2 ln u1, the angle, r*cos, r*sin = 8
+        fwd += 0.5 * (w.log + w.sqrt + w.sincos + 8.0);
         break;
       case NT_RANDU: fwd += 2.0; break;
       default: break;

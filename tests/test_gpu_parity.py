@@ -65,7 +65,8 @@ def test_philox_words_are_bit_exact(ntlib, oracle_mod):
         for q in range(0, n, 13):
             for leg in (0, 1):
                 want = oracle_mod.normal(case["path"], case["seed"], case["stream"], 2 * (case["pair0"] + q) + leg)
-                assert normals[0, q, leg] == pytest.approx(want, rel=4e-16, abs=4e-16)
+                # device Box-Muller (dedicated log/sincos, <= 2 ulp each) vs libm: a few ulp
+                assert normals[0, q, leg] == pytest.approx(want, rel=1.2e-15, abs=1.2e-15)
 
 
 def test_philox_words_many_paths(ntlib, oracle_mod):
