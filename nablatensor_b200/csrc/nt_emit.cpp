@@ -59,7 +59,11 @@ std::string lit(double x, bool f32) {
 
 class Emitter {
  public:
-  Emitter(const Tape& t, const Plan& p, const EmitConfig& cfg) : t_(t), p_(p), lp_(p.loop), cfg_(cfg) {}
+  Emitter(const Tape& t, const Plan& p, const EmitConfig& cfg)
+      : t_(t), p_(p), lp_(p.loop), cfg_(cfg),
+        // Shared-memory accumulators only while they fit in 32 KB per block
+        // (a tape with hundreds of inputs keeps them in registers instead).
+        acc_smem_(cfg.acc_smem && 2ll * (2 + t.n_in()) * t.n_out() * cfg.block * 8 <= 32 * 1024) {}
 
   std::string run();
 
@@ -68,6 +72,7 @@ class Emitter {
   const Plan& p_;
   const Loop& lp_;
   const EmitConfig& cfg_;
+  const bool acc_smem_;
   Out o_;
 
   std::string R(const char* f64, const char* f32) const { return cfg_.f32 ? f32 : f64; }
@@ -406,7 +411,7 @@ void Emitter::emit_reverse_for_output(int o) {
 void Emitter::acc_line(int32_t k, const std::string& x) {
   const std::string K = std::to_string(k);
   if (cfg_.target == 1) o_.line("nt_acc[" + K + "] += " + x + ";");
-  else if (cfg_.acc_smem) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
+  else if (acc_smem_) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
   else o_.line("nt_two_sum(&nt_acc[" + K + "], &nt_cmp[" + K + "], " + x + ");");
 }
 
@@ -517,7 +522,7 @@ std::string Emitter::run() {
   o_.line("(void)nt_gck; (void)nt_gthreads; (void)nt_tape;");
   for (int32_t j = 0; j < t_.n_in(); ++j)
     o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
-  if (cfg_.acc_smem) {
+  if (acc_smem_) {
     // Compensated accumulators live in shared memory (one column per thread):
     // they are touched once per scenario, so registers are better spent on
     // the segment buffer and occupancy.
@@ -534,7 +539,7 @@ std::string Emitter::run() {
   o_.line("const nt_u64 path = p + path_offset;");
   emit_scenario();
   o_.close();
-  if (cfg_.acc_smem) {
+  if (acc_smem_) {
     o_.line("double nt_acc[NT_CH];");
     o_.line("#pragma unroll");
     o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = NT_ACC(c) + NT_CMP(c);");
