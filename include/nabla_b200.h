@@ -232,6 +232,33 @@ int nt_dist_attach(nt_exec* exec, int32_t nranks, int32_t rank, const uint8_t id
 int nt_replay_sharded(nt_exec* exec, uint64_t total_paths, uint64_t path_offset, uint64_t seed,
                       uint64_t chunk_paths, double* sums, double* seconds);
 
+/*
+ * nt_replay without any allocation, for callers that cannot let the engine
+ * allocate device memory: a host that captures its pricing loop into a CUDA
+ * graph (cudaMalloc/cudaFree cannot be captured), or one that hands the whole
+ * device to its own memory pool under a fixed budget.  No counterpart in the
+ * reference.
+ *
+ * Launches `exec`'s kernel on the caller's stream (a cudaStream_t, NULL for
+ * the legacy default stream) over [path_offset, path_offset + paths), reading
+ * the n_in input doubles from device memory `d_inputs` and writing the
+ * n_out * (2 + n_in) sums (nt_replay's layout) to device memory `d_sums`.
+ * Returns once the work is enqueued; synchronise the stream before reading.
+ * Calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * The kernel's reduction scratch lives in a static device array of 1 MiB that
+ * every GPU loading the library holds until exit; a launch needing more
+ * (blocks x channels x 8 bytes + 256) is rejected with NT_E_INVALID_ARG.
+ * `exec` must be compiled with NT_FLAG_RECOMPUTE_ALL | NT_FLAG_SHARED_CKPT
+ * (no value tape, no global checkpoints), else NT_E_UNSUPPORTED.  All calls
+ * on a device share the scratch and keep the last call's contents: calls
+ * that overlap on the GPU race.  The first call on each device looks up the
+ * scratch address and zeroes it synchronously, so make it before any stream
+ * capture.
+ */
+int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed, const double* d_inputs,
+                      double* d_sums, void* stream);
+
 /* Enqueue-only variant for device timing: the shard dispatches plus the
  * all-reduce go to the executable's stream; results land in the device
  * accumulator (read with nt_accumulator_read). */

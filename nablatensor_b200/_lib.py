@@ -108,6 +108,8 @@ SIGNATURES = {
                          ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32), _f64p], ctypes.c_int),
     "nt_fma_peak": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
     "nt_math_probe": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
+    "nt_replay_noalloc": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
+                           ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
 
 MATH_PROBES = {0: "loop", 1: "exp(lib, |x|<=1/8)", 2: "log(lib)", 3: "sincos(lib)", 4: "sqrt(lib)",

@@ -9,10 +9,6 @@
 
 #include "nt_exec.hpp"
 
-struct nt_exec {
-  nt::Exec* impl;
-};
-
 namespace {
 
 thread_local std::string g_error;
@@ -229,6 +225,11 @@ int nt_dist_detach(nt_exec* exec) {
 extern "C" int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
                                uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals) {
   return guarded([&] { nt::philox_words(device, path0, n_paths, seed, stream, pair0, n_pairs, out, normals); });
+}
+
+extern "C" int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed,
+                                 const double* d_inputs, double* d_sums, void* stream) {
+  return guarded([&] { nt::replay_noalloc(exec, paths, path_offset, seed, d_inputs, d_sums, stream); });
 }
 
 extern "C" int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum) {

@@ -301,6 +301,24 @@ void Exec::launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, i
   ++launches;
 }
 
+unsigned Exec::grid_for(uint64_t paths) const {
+  const uint64_t need = (paths + cfg.block - 1) / cfg.block;
+  return (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(need, (uint64_t)grid));
+}
+
+void Exec::launch_external(uint64_t paths, uint64_t offset, uint64_t seed, const double* d_in, double* d_out,
+                           unsigned int* ticket, double* partials, cudaStream_t s, unsigned grid_blocks) {
+  void* gck = nullptr;
+  void* tp = nullptr;
+  const double* in = d_in;
+  int accumulate = 0;
+  unsigned long long n = paths, off = offset, sd = seed;
+  void* args[] = {&in, &n, &off, &sd, &partials, &ticket, &d_out, &accumulate, &gck, &tp};
+  cu_check(driver().launchKernel(function, grid_blocks, 1, 1, (unsigned)cfg.block, 1, 1, (unsigned)dyn_smem,
+                                 (CUstream)s, args, nullptr),
+           "cuLaunchKernel");
+}
+
 void Exec::replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, double* seconds) {
   const auto t0 = std::chrono::steady_clock::now();
   bind();

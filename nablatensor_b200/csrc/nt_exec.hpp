@@ -15,6 +15,7 @@ namespace nt {
 void cuda_check(cudaError_t e, const char* what);
 void dist_unique_id(uint8_t out[128]);
 void shard_range(uint64_t total, uint64_t offset, int32_t nranks, int32_t rank, uint64_t* from, uint64_t* count);
+size_t noalloc_scratch_bytes();
 
 struct Exec {
   std::mutex mu;
@@ -54,6 +55,11 @@ struct Exec {
   void load(int max_regs);
   void upload_inputs_if_dirty();
   void launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, int accumulate);
+  // Launch with caller-provided device pointers on a caller stream (no
+  // executable-owned buffers); `grid` blocks.
+  void launch_external(uint64_t paths, uint64_t offset, uint64_t seed, const double* d_inputs, double* d_out,
+                       unsigned int* ticket, double* partials, cudaStream_t s, unsigned grid_blocks);
+  unsigned grid_for(uint64_t paths) const;
   void replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, double* seconds);
   void accumulate(uint64_t paths, uint64_t offset, uint64_t seed);
   void read_accumulator(double* sums, bool reset);
@@ -64,4 +70,15 @@ struct Exec {
   void detach();
 };
 
+}  // namespace nt
+
+// The opaque handle behind the C ABI's nt_exec*.
+struct nt_exec {
+  nt::Exec* impl;
+};
+
+namespace nt {
+// nt_replay_noalloc (nt_noalloc.cu).
+void replay_noalloc(nt_exec* handle, uint64_t paths, uint64_t path_offset, uint64_t seed, const double* d_inputs,
+                    double* d_sums, void* stream);
 }  // namespace nt
