@@ -85,6 +85,9 @@ typedef struct nt_tape {
 #define NT_FLAG_ACC_REGS 0x20    /* keep the per-thread accumulators in registers, not shared memory */
 #define NT_FLAG_RECOMPUTE_ALL 0x40 /* reverse sweep recomputes every loop value from the step
                                       checkpoints (no per-thread value tape in global memory) */
+#define NT_FLAG_TAPE_DRAWS 0x80    /* tape only the draws and recompute exp/log/sqrt/div in the
+                                      reverse sweep (half the tape traffic); by default every
+                                      expensive loop value is taped */
 
 /*
  * Compile options: AadOptions (AadOptions.java:42-156) plus the engine knobs a
@@ -101,6 +104,7 @@ typedef struct nt_options {
   int32_t max_regs;    /* register cap per thread */
   int32_t flags;       /* NT_FLAG_* */
   int32_t fwd_unroll;  /* unroll of the forward step-unit loop */
+  int32_t grid_blocks_per_sm; /* cap on resident blocks per SM of the persistent grid */
 } nt_options;
 
 typedef struct nt_exec nt_exec;
@@ -297,8 +301,10 @@ int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops);
 /* Launches one math-probe kernel (148*4 blocks of 256 threads, `iters` calls
  * each) for instruction / flop counting under ncu: which = 0 empty loop,
  * 1 library exp, 2 library log, 3 library sincos, 4 library sqrt, 5 the
- * replay's exp, 6 its -2 ln(u1), 7 its sincos(2 pi u2), 8 library exp on a
- * wide range.  No counterpart in the reference. */
+ * replay's exp, 6 its series -2 ln(u1), 7 its series sincos(2 pi u2),
+ * 8 library exp on a wide range, 9 the table-driven -2 ln(u1), 10 the
+ * table-driven sincos(2 pi u2), 11 the radius sqrt.  No counterpart in the
+ * reference. */
 int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 
 #ifdef __cplusplus

@@ -35,6 +35,7 @@ NT_FLAG_F32_FAST = 0x8
 NT_FLAG_NO_FMAD = 0x10
 NT_FLAG_ACC_REGS = 0x20
 NT_FLAG_RECOMPUTE_ALL = 0x40
+NT_FLAG_TAPE_DRAWS = 0x80
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f64p = ctypes.POINTER(ctypes.c_double)
@@ -50,7 +51,8 @@ class NtTape(ctypes.Structure):
 class NtOptions(ctypes.Structure):
     _fields_ = [("precision", ctypes.c_int32), ("adjoints", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("block", ctypes.c_int32), ("seg_units", ctypes.c_int32), ("min_blocks", ctypes.c_int32),
-                ("max_regs", ctypes.c_int32), ("flags", ctypes.c_int32), ("fwd_unroll", ctypes.c_int32)]
+                ("max_regs", ctypes.c_int32), ("flags", ctypes.c_int32), ("fwd_unroll", ctypes.c_int32),
+                ("grid_blocks_per_sm", ctypes.c_int32)]
 
 
 class NtExecInfo(ctypes.Structure):
@@ -113,7 +115,8 @@ SIGNATURES = {
 }
 
 MATH_PROBES = {0: "loop", 1: "exp(lib, |x|<=1/8)", 2: "log(lib)", 3: "sincos(lib)", 4: "sqrt(lib)",
-               5: "exp(replay)", 6: "-2ln(u1)(replay)", 7: "sincos(2pi u2)(replay)", 8: "exp(lib, |x|<=4)"}
+               5: "exp(replay)", 6: "-2ln(u1)(series)", 7: "sincos(2pi u2)(series)", 8: "exp(lib, |x|<=4)",
+               9: "-2ln(u1)(table)", 10: "sincos(2pi u2)(table)", 11: "sqrt(replay radius)"}
 
 
 def math_probe(device: int, which: int, iters: int) -> float:
@@ -171,9 +174,9 @@ def tape_struct(tape):
 
 
 def options_struct(precision=NT_FLOAT64, adjoints=True, device=0, block=0, seg_units=0, min_blocks=0, max_regs=0,
-                   flags=0, fwd_unroll=0) -> NtOptions:
+                   flags=0, fwd_unroll=0, grid_blocks_per_sm=0) -> NtOptions:
     return NtOptions(int(precision), int(bool(adjoints)), int(device), int(block), int(seg_units), int(min_blocks),
-                     int(max_regs), int(flags), int(fwd_unroll))
+                     int(max_regs), int(flags), int(fwd_unroll), int(grid_blocks_per_sm))
 
 
 def emit_source(tape, target: int = 0, **opts) -> str:

@@ -234,7 +234,7 @@ extern "C" int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_of
 
 extern "C" int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum) {
   return guarded([&] {
-    if (which < 0 || which > 8) nt::fail(NT_E_INVALID_ARG, "which must be in [0, 8]");
+    if (which < 0 || which > 11) nt::fail(NT_E_INVALID_ARG, "which must be in [0, 11]");
     if (iters <= 0) nt::fail(NT_E_INVALID_ARG, "iters must be positive");
     nt::math_probe(device, which, iters, checksum);
   });

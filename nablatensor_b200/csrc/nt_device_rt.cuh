@@ -241,8 +241,38 @@ NT_FN double nt_exp_small(double x) {
 }
 
 NT_FN double nt_exp64(double x) {
+#ifdef NT_HOST
   if (fabs(x) <= 0.125) return nt_exp_small(x);
   return exp(x);
+#else
+  // The series always; the library exp only when some lane of the warp needs
+  // it, so a warp of GBM steps never issues the general routine.
+  double r = nt_exp_small(x);
+  const bool big = !(fabs(x) <= 0.125);
+  if (__any_sync(__activemask(), big)) {
+    if (big) r = exp(x);
+  }
+  return r;
+#endif
+}
+
+/* sqrt of a positive normal argument (the Box-Muller radius): a reciprocal
+ * square-root seed, two Newton steps, and one residual correction of the
+ * root (Markstein's method); within 1 ulp. */
+NT_FN double nt_sqrt_pos(double a) {
+#ifdef NT_HOST
+  return sqrt(a);
+#else
+  double y;
+  asm("rsqrt.approx.ftz.f64 %0, %1;" : "=d"(y) : "d"(a));
+  const double h = 0.5 * a;
+  double e = fma(-h * y, y, 0.5);
+  y = fma(y, e, y);
+  e = fma(-h * y, y, 0.5);
+  y = fma(y, e, y);
+  const double s = a * y;
+  return fma(fma(-s, s, a), 0.5 * y, s);
+#endif
 }
 
 /* EXP nodes of fp64 tapes: the dedicated routine on the device, libm in the
@@ -253,11 +283,98 @@ NT_FN double nt_exp64(double x) {
 #define NT_EXP64(x) nt_exp64(x)
 #endif
 
-/* Box-Muller legs from the dedicated routines above. */
+/* ---- table-driven Box-Muller ---------------------------------------------
+ * Short polynomials on a small reduced range plus tabulated values
+ * (nt_math_tables.cuh, generated in 60-digit decimal arithmetic): fewer and
+ * shorter dependent chains than the series above.  On the device every block
+ * stages the tables in shared memory (nt_math_tables_load) before its first
+ * draw; the host build reads the constant arrays. */
+#ifdef NT_HOST
+#define NT_TABLE_QUAL const
+#else
+#define NT_TABLE_QUAL __device__ const
+#endif
+#include "nt_math_tables.cuh"
+
+#ifdef NT_HOST
+#define NT_LN_TAB nt_ln_tab_g
+#define NT_SC_TAB nt_sc_tab_g
+NT_FN void nt_math_tables_load(void) {}
+#else
+__shared__ double nt_ln_tab_s[NT_LN_TAB_N * 3];
+__shared__ double nt_sc_tab_s[NT_SC_TAB_N * 2];
+#define NT_LN_TAB nt_ln_tab_s
+#define NT_SC_TAB nt_sc_tab_s
+/* Every thread of the block must call this before any Box-Muller draw. */
+NT_FN void nt_math_tables_load(void) {
+  for (int i = threadIdx.x; i < NT_LN_TAB_N * 3; i += blockDim.x) nt_ln_tab_s[i] = nt_ln_tab_g[i];
+  for (int i = threadIdx.x; i < NT_SC_TAB_N * 2; i += blockDim.x) nt_sc_tab_s[i] = nt_sc_tab_g[i];
+  __syncthreads();
+}
+#endif
+
+/* -2 ln(u1) by Tang's table method (ACM TOMS 15(2), 1989): u1 = m 2^k with m
+ * folded into [0.75, 1.5); c_j = 0.75 + j/128 the nearest centre (c_32 = 1
+ * exactly, so u1 near 1 keeps full relative precision); f = m - c_j exact;
+ * t = f / c_j, |t| <= 1/192; ln(1 + t) to t^7 (truncation < 2^-60);
+ * ln c_j tabulated as a double-double. */
+NT_FN double nt_neg2log_u1_t(nt_u32 w0) {
+  const double u = ((double)w0 + 0.5) * NT_UINT_SCALE;
+  const int hi = nt_hiword(u);
+  int k = ((hi >> 20) & 0x7ff) - 1023;
+  int mhi = (hi & 0x000fffff) | 0x3ff00000; /* m in [1, 2) */
+  if (mhi >= 0x3ff80000) {                   /* m >= 1.5: use m / 2 in [0.75, 1) */
+    mhi -= 0x00100000;
+    k += 1;
+  }
+  const double m = nt_from_words(mhi, nt_loword(u));
+  const int j = (int)((m - 0.75) * 128.0 + 0.5);
+  const double f = m - (0.75 + (double)j * 0.0078125); /* exact */
+  const double* e = &NT_LN_TAB[3 * j];
+  const double t = f * e[0];
+  double p = 1.0 / 7.0;
+  p = fma(p, t, -1.0 / 6.0);
+  p = fma(p, t, 1.0 / 5.0);
+  p = fma(p, t, -0.25);
+  p = fma(p, t, 1.0 / 3.0);
+  p = fma(p, t, -0.5);
+  const double l1p = fma(t * t, p, t);
+  const double kd = (double)k;
+  const double s1 = fma(kd, 0x1.62e42p-1 /* ln2 hi */, e[1]);
+  const double s2 = fma(kd, 0x1.fdf473de6af28p-22 /* ln2 lo */, e[2] + l1p);
+  return -2.0 * (s1 + s2);
+}
+
+/* sin and cos of the reference's angle theta = fl(2 pi u2): theta = a_j + b
+ * with a_j = j pi/128 tabulated, b in [0, pi/128) (pi/128 in two parts, j*hi
+ * exact); sin b to b^7 and cos b - 1 to b^6 (truncation < 2^-61). */
+NT_FN void nt_sincos_2pi_u2_t(nt_u32 w1, double* sn, double* cs) {
+  const double u2 = ((double)w1 + 0.5) * NT_UINT_SCALE;
+  const double th = NT_TWO_PI * u2;
+  int j = (int)(th * NT_128_OVER_PI);
+  if (j > NT_SC_TAB_N - 1) j = NT_SC_TAB_N - 1;
+  const double jd = (double)j;
+  double b = fma(-jd, NT_PI_128_HI, th);
+  b = fma(-jd, NT_PI_128_LO, b);
+  const double z = b * b;
+  double ps = -1.0 / 5040.0;
+  ps = fma(ps, z, 1.0 / 120.0);
+  ps = fma(ps, z, -1.0 / 6.0);
+  const double sb = fma(b * z, ps, b);
+  double pc = -1.0 / 720.0;
+  pc = fma(pc, z, 1.0 / 24.0);
+  pc = fma(pc, z, -0.5);
+  const double cm1 = z * pc;
+  const double S = NT_SC_TAB[2 * j], C = NT_SC_TAB[2 * j + 1];
+  *sn = S + fma(C, sb, S * cm1);
+  *cs = C + fma(C, cm1, -S * sb);
+}
+
+/* Box-Muller legs from the table-driven routines. */
 NT_FN void nt_bm64_words(nt_u32 w0, nt_u32 w1, double* cos_leg, double* sin_leg) {
-  const double r = sqrt(nt_neg2log_u1(w0));
+  const double r = nt_sqrt_pos(nt_neg2log_u1_t(w0));
   double s, c;
-  nt_sincos_2pi_u2(w1, &s, &c);
+  nt_sincos_2pi_u2_t(w1, &s, &c);
   *cos_leg = r * c;
   *sin_leg = r * s;
 }
@@ -357,6 +474,15 @@ NT_FN double nt_from_bits64(nt_u64 bits) {
   return x;
 #else
   return __longlong_as_double((long long)bits);
+#endif
+}
+
+/* Hint the line holding *p into L2 ahead of its load (no register, no wait). */
+NT_FN void nt_prefetch_l2(const void* p) {
+#ifdef NT_HOST
+  (void)p;
+#else
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 #endif
 }
 

@@ -379,6 +379,18 @@ void Emitter::emit_reverse_for_output(int o) {
     for (int32_t c = 0; c < nck; ++c)
       o_.line("const real cs" + std::to_string(lp_.ckpt[c]) + " = NT_CK(s * " + std::to_string(nck) + " + " +
               std::to_string(c) + ");");
+    if (lp_.n_tape > 0 && cfg_.target == 0) {
+      // The previous segment's tape lines head for L2 while this one is reversed.
+      o_.open("if (s > 0) {");
+      for (int g = 0; g < G; ++g)
+        for (int32_t k = 0; k < lp_.n_tape; ++k)
+          o_.line("nt_prefetch_l2(&NT_TAPE((s - 1) * " + std::to_string(G) + " + " + std::to_string(g) + ", " +
+                  std::to_string(k) + "));");
+      if (cfg_.global_ckpt)
+        for (int32_t c = 0; c < nck; ++c)
+          o_.line("nt_prefetch_l2(&NT_CK((s - 1) * " + std::to_string(nck) + " + " + std::to_string(c) + "));");
+      o_.close();
+    }
     for (int g = 0; g < G; ++g) {
       std::string decl;
       for (int32_t j = 0; j < L; ++j)
@@ -535,6 +547,7 @@ std::string Emitter::run() {
     o_.line("#pragma unroll");
     o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
   }
+  o_.line("nt_math_tables_load();");
   o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
   o_.line("const nt_u64 path = p + path_offset;");
   emit_scenario();

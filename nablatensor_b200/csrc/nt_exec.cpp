@@ -205,6 +205,7 @@ void Exec::load(int max_regs) {
   int per_sm = 0;
   cu_check(d.occupancy(&per_sm, function, cfg.block, (size_t)dyn_smem), "cuOccupancyMaxActiveBlocksPerMultiprocessor");
   if (per_sm < 1) fail(NT_E_CUDA, "kernel does not fit on an SM");
+  if (cfg.grid_blocks_per_sm > 0) per_sm = std::min(per_sm, cfg.grid_blocks_per_sm);
   blocks_per_sm = per_sm;
   grid = sm_count * per_sm;
   cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");

@@ -103,6 +103,8 @@ struct EmitConfig {
   bool fmad = true;        // allow multiply-add contraction
   bool acc_smem = true;    // compensated accumulators in shared memory
   bool tape = true;        // expensive loop values go to a per-thread tape instead of being recomputed
+  bool tape_all = true;    // tape draws and transcendentals (else draws only)
+  int32_t grid_blocks_per_sm = 0;  // 0: as many as fit
   int32_t fwd_unroll = 1;  // unroll of the forward unit loop
   int32_t block = 128;
   int32_t min_blocks = 0;
@@ -123,6 +125,7 @@ std::string emit(const Tape& t, const Plan& p, const EmitConfig& cfg);
 int32_t ckpt_values(const Plan& p);
 
 extern const char* kDeviceRuntimeSource;  // nt_device_rt.cuh, embedded at build time
+extern const char* kMathTablesSource;     // nt_math_tables.cuh, embedded at build time
 
 // Frozen flop weights of the fp64 transcendentals {exp, log, sqrt, sincos}
 // (nt_flops.cpp), used for the algorithmic flop count of a tape.

@@ -10,6 +10,7 @@ namespace {
 
 __global__ void kat_kernel(nt_u64 path0, unsigned n_paths, nt_u64 seed, int stream, unsigned pair0,
                            unsigned n_pairs, unsigned* out, double* normals) {
+  nt_math_tables_load();  // every thread, before the bounds check
   const nt_u64 idx = (nt_u64)blockIdx.x * blockDim.x + threadIdx.x;
   const nt_u64 total = (nt_u64)n_paths * n_pairs;
   if (idx >= total) return;
@@ -84,6 +85,7 @@ __device__ __forceinline__ unsigned probe_word(unsigned x) {
 }
 
 __global__ void __launch_bounds__(256) math_probe_kernel(int which, int iters, double* out) {
+  nt_math_tables_load();
   const unsigned tid = blockIdx.x * blockDim.x + threadIdx.x;
   double acc = 0.0, acc2 = 0.0;
   for (int i = 0; i < iters; ++i) {
@@ -100,6 +102,9 @@ __global__ void __launch_bounds__(256) math_probe_kernel(int which, int iters, d
       case 6: acc += nt_neg2log_u1(w); break;                         // dedicated -2 ln u1
       case 7: nt_sincos_2pi_u2(w, &s, &c); acc += s; acc2 += c; break;  // dedicated sincos
       case 8: acc += exp((u - 0.5) * 8.0); break;                     // library exp, wide range
+      case 9: acc += nt_neg2log_u1_t(w); break;                       // table-driven -2 ln u1
+      case 10: nt_sincos_2pi_u2_t(w, &s, &c); acc += s; acc2 += c; break;  // table-driven sincos
+      case 11: acc += nt_sqrt_pos(u * 46.0); break;                   // the replay's radius sqrt
       default: break;
     }
   }

@@ -71,8 +71,8 @@ std::vector<char> nvrtc_compile(const std::string& source, const std::string& ar
       "--extra-device-vectorization",
       "-lineinfo",
   };
-  std::string key_text = source + "\x01" + kDeviceRuntimeSource + "\x01" + std::to_string(major) + "." +
-                         std::to_string(minor);
+  std::string key_text = source + "\x01" + kDeviceRuntimeSource + "\x01" + kMathTablesSource + "\x01" +
+                         std::to_string(major) + "." + std::to_string(minor);
   for (auto& o : opts) key_text += "\x02" + o;
   const uint64_t key = fnv1a(key_text);
   if (seconds) *seconds = 0.0;
@@ -97,9 +97,9 @@ std::vector<char> nvrtc_compile(const std::string& source, const std::string& ar
   }
   const auto t0 = std::chrono::steady_clock::now();
   nvrtcProgram prog;
-  const char* hdr_src[] = {kDeviceRuntimeSource};
-  const char* hdr_name[] = {"nt_device_rt.cuh"};
-  check(nvrtcCreateProgram(&prog, source.c_str(), "nt_replay.cu", 1, hdr_src, hdr_name), "nvrtcCreateProgram");
+  const char* hdr_src[] = {kDeviceRuntimeSource, kMathTablesSource};
+  const char* hdr_name[] = {"nt_device_rt.cuh", "nt_math_tables.cuh"};
+  check(nvrtcCreateProgram(&prog, source.c_str(), "nt_replay.cu", 2, hdr_src, hdr_name), "nvrtcCreateProgram");
   std::vector<const char*> copts;
   for (auto& o : opts) copts.push_back(o.c_str());
   nvrtcResult rc = nvrtcCompileProgram(prog, (int)copts.size(), copts.data());

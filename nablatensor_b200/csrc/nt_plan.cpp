@@ -293,6 +293,9 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   cfg.fwd_unroll = opt->fwd_unroll > 0 ? opt->fwd_unroll : 1;
   cfg.acc_smem = (opt->flags & NT_FLAG_ACC_REGS) == 0;
   cfg.tape = (opt->flags & NT_FLAG_RECOMPUTE_ALL) == 0;
+  cfg.tape_all = (opt->flags & NT_FLAG_TAPE_DRAWS) == 0;
+  if (opt->grid_blocks_per_sm < 0) fail(NT_E_INVALID_ARG, "grid_blocks_per_sm must be >= 0");
+  cfg.grid_blocks_per_sm = opt->grid_blocks_per_sm;
   return cfg;
 }
 
@@ -332,8 +335,29 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     if (odd_base && odd_stride) { B += L; N -= 1; }  // peel one iteration into the prologue
     int32_t units = N / U;
     // Units per checkpoint segment: a divisor of the unit count close to the
-    // target; otherwise the remainder units are peeled into the epilogue.
-    const int32_t target = cfg.seg_units > 0 ? cfg.seg_units : std::max(1, 8 / U);
+    // target; otherwise the remainder units are peeled into the epilogue.  The
+    // automatic target keeps one segment's reverse-sweep values within about
+    // 64 registers (the values a unit's reverse reads, 2 registers each in fp64).
+    int32_t per_unit = 0;
+    if (units >= 2 && validate(t, B, L * U, nullptr) >= 2) {
+      Loop probe;
+      probe.present = true;
+      probe.B = B;
+      probe.L = L * U;
+      probe.N = units;
+      describe(t, probe);
+      std::vector<uint8_t> kept(probe.L, 0);
+      std::vector<Ref> rd;
+      for (int32_t j = 0; j < probe.L; ++j) {
+        reverse_reads(probe, j, rd);
+        for (const Ref& r : rd)
+          if (r.kind == REF_SAME || r.kind == REF_CARRY) kept[r.idx] = 1;
+      }
+      for (uint8_t k : kept) per_unit += k;
+    }
+    const int32_t words = cfg.f32 ? 1 : 2;
+    const int32_t auto_target = per_unit > 0 ? std::max(1, std::min(16, 64 / (per_unit * words))) : std::max(1, 8 / U);
+    const int32_t target = cfg.seg_units > 0 ? cfg.seg_units : auto_target;
     int32_t G = target;
     if (units >= 2) {
       int32_t bestG = -1;
@@ -381,7 +405,8 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     // leaf: the forward sweep writes its value to the thread's tape and the
     // reverse sweep reads it back instead of recomputing its inputs.
     auto expensive = [&](int op) {
-      return op == NT_RANDN || op == NT_RANDU || op == NT_EXP || op == NT_LOG || op == NT_SQRT || op == NT_DIV;
+      if (op == NT_RANDN || op == NT_RANDU) return true;
+      return cfg.tape_all && (op == NT_EXP || op == NT_LOG || op == NT_SQRT || op == NT_DIV);
     };
     std::vector<uint8_t> need(lp.stored);
     lp.tape_slot.assign(L, -1);

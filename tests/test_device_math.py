@@ -33,6 +33,7 @@ static double ulp_of(double x) {
 int main(void) {
   uint64_t st = 0x9E3779B97F4A7C15ull;
   double worst_log = 0, worst_sin = 0, worst_cos = 0, worst_exp = 0;
+  double worst_log_t = 0, worst_sin_t = 0, worst_cos_t = 0;
   const uint32_t edges[] = {0u, 1u, 2u, 0x7fffffffu, 0x80000000u, 0xffffffffu, 0xfffffffeu, 0x3fffffffu,
                             0x40000000u, 0xbfffffffu, 0xc0000000u, 0x6a09e667u, 0xb504f333u, 0xb504f334u,
                             0x20000000u, 0x60000000u, 0xa0000000u, 0xe0000000u};
@@ -56,13 +57,23 @@ int main(void) {
     double ec = fabsl((long double)c - wc) / fmax(ulp_of((double)wc), 1.1102230246251565e-16);
     if (es > worst_sin) worst_sin = es;
     if (ec > worst_cos) worst_cos = ec;
+    /* the table-driven versions (what the device Box-Muller calls) */
+    const double got_lt = nt_neg2log_u1_t(w);
+    e = fabsl((long double)got_lt - want_l) / ulp_of((double)want_l);
+    if (e > worst_log_t) worst_log_t = e;
+    nt_sincos_2pi_u2_t(w, &s, &c);
+    es = fabsl((long double)s - ws) / fmax(ulp_of((double)ws), 1.1102230246251565e-16);
+    ec = fabsl((long double)c - wc) / fmax(ulp_of((double)wc), 1.1102230246251565e-16);
+    if (es > worst_sin_t) worst_sin_t = es;
+    if (ec > worst_cos_t) worst_cos_t = ec;
     /* exp on [-1/8, 1/8] */
     const double x = ((double)w / 4294967295.0 - 0.5) * 0.25;
     const long double we = expl((long double)x);
     double ee = fabsl((long double)nt_exp_small(x) - we) / ulp_of((double)we);
     if (ee > worst_exp) worst_exp = ee;
   }
-  printf("%.6f %.6f %.6f %.6f\n", worst_log, worst_sin, worst_cos, worst_exp);
+  printf("%.6f %.6f %.6f %.6f %.6f %.6f %.6f\n", worst_log, worst_sin, worst_cos, worst_exp, worst_log_t,
+         worst_sin_t, worst_cos_t);
   return 0;
 }
 """
@@ -78,11 +89,15 @@ def worst():
     subprocess.run(["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-I",
                     os.path.join(ROOT, "nablatensor_b200", "csrc"), "-o", exe, src, "-lm"], check=True)
     out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()
-    return dict(zip(["log", "sin", "cos", "exp"], map(float, out)))
+    return dict(zip(["log", "sin", "cos", "exp", "log_t", "sin_t", "cos_t"], map(float, out)))
 
 
 def test_neg2log_u1_within_2_ulp(worst):
     assert worst["log"] <= 2.0, worst
+
+
+def test_table_driven_box_muller_within_2_ulp(worst):
+    assert worst["log_t"] <= 2.0 and worst["sin_t"] <= 2.0 and worst["cos_t"] <= 2.0, worst
 
 
 def test_sincos_within_2_ulp(worst):

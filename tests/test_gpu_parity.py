@@ -174,15 +174,19 @@ def test_shared_checkpoints_and_recompute_all_agree(engine):
     tape = quant.asian_tape(252)
     with engine.compile(tape, FP64) as a, \
             engine.compile(tape, FP64.with_engine_option("cuda", "sharedCheckpoints", "true")) as b, \
-            engine.compile(tape, FP64.with_engine_option("cuda", "recomputeAll", "true")) as c:
-        assert a.info()["ckpt_global"] == 1 and a.info()["tape_slots"] == 4
+            engine.compile(tape, FP64.with_engine_option("cuda", "recomputeAll", "true")) as c, \
+            engine.compile(tape, FP64.with_engine_option("cuda", "tapeDraws", "true")) as d:
+        assert a.info()["ckpt_global"] == 1 and a.info()["tape_slots"] == 4  # normals and exps per unit
         assert b.info()["ckpt_global"] == 0
         assert c.info()["tape_slots"] == 0
+        assert d.info()["tape_slots"] == 2  # the two normals only
         x, _ = a.replay_sums(30_000, 5, 6)
         y, _ = b.replay_sums(30_000, 5, 6)
         z, _ = c.replay_sums(30_000, 5, 6)
+        w, _ = d.replay_sums(30_000, 5, 6)
     np.testing.assert_allclose(x, y, rtol=1e-15)
     np.testing.assert_allclose(x, z, rtol=2e-12)
+    np.testing.assert_allclose(x, w, rtol=2e-12)
 
 
 @pytest.mark.parametrize("make,inputs,seed", [
