@@ -5,7 +5,12 @@ scenario ranges sharded across the GPUs with one NCCL all-reduce of the
 7 fp64 accumulators.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload asian1e9|asian2m|barrier20m|basket10m]
     torchrun --nproc-per-node N bench.py --gpus N ...
+
+The default workload is config 3 above; `--workload` times the other
+BASELINE configurations (1: Asian 2M, 2: fp32 barrier 20M, 4: 10-asset
+basket 10M) with the same JSON line.
 
 Prints one JSON line on rank 0.  `value` is whole-job scenarios/s timed with
 CUDA events on the engine's stream (inputs resident, max over ranks); `e2e`
@@ -37,6 +42,48 @@ METRIC = "scenarios/s (value+all Greeks, one adjoint sweep) at 1/2/4/8 B200; % F
 ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
 SEED = 42
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+class Workload:
+    """One BASELINE configuration: the tape, its inputs, precision and size.
+    `cpu_share` scales the CPU sample so each workload's CPU leg does about
+    the same amount of interpreter work (the basket tape is ~8x the Asian)."""
+
+    def __init__(self, name, config, tape, inputs, f32, paths, chunk, seed, cpu_share, desc, profile):
+        self.name, self.config, self._tape, self._inputs = name, config, tape, inputs
+        self.f32, self.paths, self.chunk, self.seed = f32, paths, chunk, seed
+        self.cpu_share, self.desc, self.profile = cpu_share, desc, profile
+
+    def tape(self):
+        from nablatensor_b200 import quant
+        return self._tape(quant)
+
+    def inputs(self, tape):
+        return list(self._inputs) if self._inputs is not None else list(tape.recordedInputs())
+
+    @property
+    def dtype(self):
+        return "f32" if self.f32 else "f64"
+
+
+WORKLOADS = {w.name: w for w in [
+    Workload("asian1e9", 3, lambda q: q.asian_tape(252), ATM, False, 1e9, 1 << 27, SEED, 1.0,
+             "BASELINE config 3: fp64 Asian call, GBM S0=K=100 sigma=0.2 r=0.03 T=1, 252 steps, value + 5 Greeks "
+             "from one adjoint sweep, 1e9 scenarios per step, seed 42, shards + 1 NCCL all-reduce of 7 fp64",
+             "asian_fp64_replay_ncu.md"),
+    Workload("asian2m", 1, lambda q: q.asian_tape(252), ATM, False, 2e6, 0, SEED, 1.0,
+             "BASELINE config 1: fp64 Asian call, GBM S0=K=100 sigma=0.2 r=0.03 T=1, 252 steps, value + 5 Greeks, "
+             "2,000,000 scenarios per step, seed 42", "asian_fp64_replay_ncu.md"),
+    Workload("barrier20m", 2, lambda q: q.barrier_tape(252), ATM, True, 2e7, 0, SEED, 0.5,
+             "BASELINE config 2: fp32 down-and-in barrier call, barrier 80 monitored at 252 steps, S0=K=100 "
+             "sigma=0.2 r=0.03 T=1, value + 5 Greeks, 20,000,000 scenarios per step, seed 42 (fp32 nodes; "
+             "exp/log/Box-Muller evaluated in fp64 and narrowed, the reference's fp32 semantics)",
+             "barrier_fp32_replay_ncu.md"),
+    Workload("basket10m", 4, lambda q: q.basket_tape(), None, False, 1e7, 0, 7, 0.12,
+             "BASELINE config 4: fp64 10-asset basket call, Cholesky of equicorrelation rho=0.5, spots U[80,120] "
+             "and vols U[0.15,0.40] from seed 7, equal weights, K=100 r=0.03 T=1, 52 weekly steps, value + 21 "
+             "Greeks, 10,000,000 scenarios per step, seed 7", "basket_fp64_replay_ncu.md"),
+]}
 
 
 def _env_int(name, default):
@@ -91,42 +138,49 @@ class ClockSampler:
                 "samples_under_load": len(sm)}
 
 
-def cpu_baseline(paths: int, threads: int = 0) -> dict:
+def _cpu_sample(args, wl: Workload) -> int:
+    return max(10_000, int(args.cpu_sample * wl.cpu_share))
+
+
+def cpu_baseline(wl: Workload, paths: int, threads: int = 0) -> dict:
     """The CPU oracle (port of ScalarReplay + Philox) on all host threads."""
     from oracle import oracle as O
-    t = O.asian_tape(252)
+    tape = wl.tape()
+    t, x = O.FlatTape.of(tape), wl.inputs(tape)
     cores = threads or os.cpu_count()
-    O.replay(t, ATM, 10_000, 0, SEED, threads=cores)  # warm
+    O.replay(t, x, 10_000, 0, wl.seed, f32=wl.f32, threads=cores)  # warm
     t0 = time.perf_counter()
-    O.replay(t, ATM, paths, 0, SEED, threads=cores)
+    O.replay(t, x, paths, 0, wl.seed, f32=wl.f32, threads=cores)
     secs = time.perf_counter() - t0
     return {"value": paths / secs, "unit": "scenarios/s", "cores": cores, "kind": "port",
-            "sample": f"{paths} scenarios of the 252-step Asian fp64 tape (value + 5 Greeks), seed {SEED}, "
-                      f"scalar interpreter on {cores} threads, {secs:.2f} s"}
+            "sample": f"{paths} scenarios of the {wl.name} tape ({tape.size()} nodes, {wl.dtype}, value + "
+                      f"{tape.input_count()} Greeks), seed {wl.seed}, scalar interpreter on {cores} threads, "
+                      f"{secs:.2f} s"}
 
 
-def run_reference(args, rank: int) -> None:
+def run_reference(args, rank: int, wl: Workload) -> None:
     if rank != 0:
         return
     from oracle import oracle as O
-    t = O.asian_tape(252)
+    tape = wl.tape()
+    t, x = O.FlatTape.of(tape), wl.inputs(tape)
     cores = os.cpu_count()
-    sample = args.cpu_sample
+    sample = _cpu_sample(args, wl)
     for w in range(args.warmup):
-        O.replay(t, ATM, max(10_000, sample // 10), w * sample, SEED, threads=cores)
+        O.replay(t, x, max(10_000, sample // 10), w * sample, wl.seed, f32=wl.f32, threads=cores)
     times = []
     for k in range(args.steps):
         t0 = time.perf_counter()
-        O.replay(t, ATM, sample, k * sample, SEED, threads=cores)
+        O.replay(t, x, sample, k * sample, wl.seed, f32=wl.f32, threads=cores)
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = args.steps * sample / total
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "scenarios/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "asian_call_fp64_252steps_value+5greeks (BASELINE config 3 tape; CPU sample per step)",
-                   "paths_per_step": sample, "seed": SEED},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+        "config": {"workload": f"{wl.name}: {wl.desc} (CPU sample of {sample} scenarios per step)",
+                   "paths_per_step": sample, "seed": wl.seed},
         "cpu_baseline": {"value": value, "unit": "scenarios/s", "cores": cores, "kind": "port",
                          "sample": f"{sample} scenarios per step; reference is Java (no JVM on this host), "
                                    f"timed: C restatement of its scalar `cpu` engine"},
@@ -135,7 +189,7 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None:
     import torch
     import torch.distributed as dist
     from nablatensor_b200 import _lib, quant
@@ -158,17 +212,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    tape = quant.asian_tape(252)
-    ex = CudaAadEngine(device=local_rank).compile(tape, AadOptions(precision=PrecisionEnum.FLOAT64))
+    tape = wl.tape()
+    x = wl.inputs(tape)
+    precision = PrecisionEnum.FLOAT32 if wl.f32 else PrecisionEnum.FLOAT64
+    ex = CudaAadEngine(device=local_rank).compile(tape, AadOptions(precision=precision))
+    ex.setInputs(x)
     info = ex.info()
     if world > 1:
         uid = [dist_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ex.distAttach(world, rank, uid[0], timeout_ms=120_000)
-    peak64 = _lib.fma_peak(local_rank, True)
+    peak = _lib.fma_peak(local_rank, not wl.f32)
 
-    total = int(args.paths)
-    chunk = int(args.chunk)
+    total = int(args.paths if args.paths is not None else wl.paths)
+    chunk = int(args.chunk if args.chunk is not None else wl.chunk)
+    seed = wl.seed
     first, mine = _lib.shard_range(total, 0, world, rank)
     launches_per_step = -(-mine // chunk) if chunk > 0 else 1
     h = ex._handle()
@@ -177,7 +235,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     sums = np.zeros(info["channels"], dtype=np.float64)
 
     def step(offset):
-        _lib.check(_lib.lib().nt_replay_sharded_async(h, total, offset, SEED, chunk))
+        _lib.check(_lib.lib().nt_replay_sharded_async(h, total, offset, seed, chunk))
 
     for _ in range(args.warmup):
         step(0)
@@ -209,8 +267,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for k in range(args.steps):
         barrier()
         t0 = time.perf_counter()
-        ex.setInputs(ATM)  # host -> device copy of the 5 inputs
-        r = ex.replaySharded(total, 0, SEED, chunk)  # launches + all-reduce + device -> host sums
+        ex.setInputs(x)  # host -> device copy of the inputs
+        r = ex.replaySharded(total, 0, seed, chunk)  # launches + all-reduce + device -> host sums
         e2e_times.append(time.perf_counter() - t0)
     e2e_total = max_over_ranks(sum(e2e_times))
     e2e_value = args.steps * total / e2e_total
@@ -220,28 +278,26 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     kernel_s = (my_total_ms * 1e-3) / (args.steps * launches_per_step)
     paths_per_launch = mine / launches_per_step
     achieved = flops_per_scen * paths_per_launch / kernel_s / 1e12
-    roofline = {"bound": "fp64", "achieved": achieved, "peak": peak64, "unit": "TFLOP/s", "frac": achieved / peak64,
-                "peak_source": "measured DFMA peak on this GPU (nt_fma_peak, of measured)",
-                "flops_per_scenario": flops_per_scen, "traffic": _profiled_traffic(paths_per_launch)}
+    roofline = {"bound": wl.dtype.replace("f", "fp"), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_source": f"measured {'FFMA' if wl.f32 else 'DFMA'} peak on this GPU (nt_fma_peak, of measured)",
+                "flops_per_scenario": flops_per_scen, "traffic": _profiled_traffic(wl, paths_per_launch)}
 
     line = None
     if rank == 0:
-        cpu = cpu_baseline(args.cpu_sample) if world == 1 else None
+        cpu = cpu_baseline(wl, _cpu_sample(args, wl)) if world == 1 else None
         line = {
             "metric": METRIC, "value": value, "unit": "scenarios/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "BASELINE config 3: fp64 Asian call, GBM S0=K=100 sigma=0.2 r=0.03 T=1, "
-                                   "252 steps, value + 5 Greeks from one adjoint sweep, 1e9 scenarios per step, "
-                                   "seed 42, shards + 1 NCCL all-reduce of 7 fp64",
-                       "paths_per_step": total, "chunk_paths": chunk, "l2": "flushed between timed steps "
-                       "(256 MiB write); inputs are 40 bytes", "kernel": {k: info[k] for k in (
+            "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+            "config": {"workload": f"{wl.name}: {wl.desc}", "paths_per_step": total, "chunk_paths": chunk, "l2": "flushed between timed steps "
+                       f"(256 MiB write); inputs are {8 * len(x)} bytes", "kernel": {k: info[k] for k in (
                            "registers", "local_bytes", "blocks_per_sm", "grid", "loop_units", "seg_units",
                            "segments", "ckpt_slots", "stored_per_unit")},
                        "price": res.value(), "greeks": dict(zip(tape.input_names, map(float, res.gradients())))},
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "scenarios/s", "h2d_bytes_per_step": 8 * len(ATM),
+            "e2e": {"value": e2e_value, "unit": "scenarios/s", "h2d_bytes_per_step": 8 * len(x),
                     "d2h_bytes_per_step": 8 * info["channels"]},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clk,
@@ -255,10 +311,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         print(json.dumps(line), flush=True)
 
 
-def _profiled_traffic(paths_per_launch: float):
-    """DRAM bytes per launch from the committed ncu summary, scaled by the
-    scenarios one launch processes (null when no capture is committed)."""
-    path = os.path.join(ROOT, "profiles", "asian_fp64_replay_ncu.md")
+def _profiled_traffic(wl: Workload, paths_per_launch: float):
+    """DRAM bytes per launch from the workload's committed ncu summary, scaled
+    by the scenarios one launch processes (null when no capture is committed)."""
+    path = os.path.join(ROOT, "profiles", wl.profile)
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_scenario:"):
@@ -274,8 +330,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--paths", type=float, default=1e9)
-    ap.add_argument("--chunk", type=int, default=1 << 27)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="asian1e9",
+                    help="BASELINE configuration to time (default: config 3, the headline)")
+    ap.add_argument("--paths", type=float, default=None, help="scenarios per step (default: the workload's)")
+    ap.add_argument("--chunk", type=int, default=None, help="scenarios per launch (default: the workload's)")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000)
     ap.add_argument("--math-probes", action="store_true",
                     help="launch each math-probe kernel once (for ncu per-call instruction/flop counts)")
@@ -290,10 +348,11 @@ def main():
     world = _env_int("WORLD_SIZE", 1)
     local_rank = _env_int("LOCAL_RANK", 0)
     args.warmup = max(3, args.warmup)  # the timing rules ask for at least 3 warm-up steps
+    wl = WORKLOADS[args.workload]
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, wl)
     else:
-        run_ours(args, rank, world, local_rank)
+        run_ours(args, rank, world, local_rank, wl)
 
 
 if __name__ == "__main__":

@@ -205,6 +205,97 @@ class ExoticProducts:
         return record
 
 
+class CorrelatedNormals:
+    """CorrelatedNormals.java:36-93: lower Cholesky factor of a correlation
+    matrix; mix() records y = L z node by node."""
+
+    def __init__(self, lower):
+        self.lower = lower
+
+    @staticmethod
+    def of(corr) -> "CorrelatedNormals":
+        n = len(corr)
+        lo = [[0.0] * n for _ in range(n)]
+        for i in range(n):
+            for j in range(i + 1):
+                s = float(corr[i][j])
+                for k in range(j):
+                    s -= lo[i][k] * lo[j][k]
+                if i == j:
+                    if s <= 0.0:
+                        raise ValueError(f"correlation matrix is not positive definite at index {i}")
+                    lo[i][j] = math.sqrt(s)
+                else:
+                    lo[i][j] = s / lo[j][j]
+        return CorrelatedNormals(lo)
+
+    def size(self) -> int:
+        return len(self.lower)
+
+    def mix(self, rec: AadRecorder, z: Sequence[ADouble]) -> List[ADouble]:
+        y = []
+        for i in range(len(self.lower)):
+            acc = rec.constant(0.0)
+            for j in range(i + 1):
+                acc = acc.add(z[j].mul(self.lower[i][j]))
+            y.append(acc)
+        return y
+
+    def draw(self, rec: AadRecorder) -> List[ADouble]:
+        return self.mix(rec, [rec.randn() for _ in range(len(self.lower))])
+
+
+def equicorrelation(n: int, rho: float):
+    return [[1.0 if i == j else rho for j in range(n)] for i in range(n)]
+
+
+class BasketOption:
+    """An n-asset arithmetic basket option under correlated GBM.  The reference
+    fixes the basket at 3 assets (BasketOption.java:35-76); this records the
+    same per-step shape for any n: market inputs s_1..s_n, v_1..v_n, rate (in
+    that order), a Cholesky mix of n fresh normals per step, then per asset
+    s_i *= exp(drift_i + v_i sqrt(dt) y_i)."""
+
+    @staticmethod
+    def record(rec: AadRecorder, spots, vols, rate: float, weights, strike: float, corr, maturity: float,
+               steps: int, kind: OptionType = OptionType.CALL) -> None:
+        n = len(spots)
+        mixer = CorrelatedNormals.of(corr)
+        dt = maturity / steps
+        sqrt_dt = math.sqrt(dt)
+        s = [rec.input(f"s{i + 1}", float(spots[i])) for i in range(n)]
+        vol = [rec.input(f"v{i + 1}", float(vols[i])) for i in range(n)]
+        r = rec.input("rate", float(rate))
+        drift = [r.sub(vol[i].mul(vol[i]).mul(0.5)).mul(dt) for i in range(n)]
+        for _ in range(steps):
+            z = mixer.draw(rec)
+            for i in range(n):
+                s[i] = s[i].mul(drift[i].add(vol[i].mul(sqrt_dt).mul(z[i])).exp())
+        level = rec.constant(0.0)
+        for i in range(n):
+            level = level.add(s[i].mul(float(weights[i])))
+        intrinsic = level.sub(strike).max(0.0) if kind == OptionType.CALL else rec.constant(strike).sub(level).max(0.0)
+        rec.output(intrinsic.mul(r.neg().mul(maturity).exp()))
+
+
+def basket_config4_market(n: int = 10, seed: int = 7):
+    """BASELINE config 4 market: spots ~ U[80, 120] and vols ~ U[0.15, 0.40],
+    drawn with numpy's PCG64 generator seeded 7 (spots first, then vols)."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    spots = g.uniform(80.0, 120.0, n)
+    vols = g.uniform(0.15, 0.40, n)
+    return [float(x) for x in spots], [float(x) for x in vols]
+
+
+def basket_tape(n: int = 10, steps: int = 52, rho: float = 0.5, seed: int = 7, strike: float = 100.0,
+                rate: float = 0.03, maturity: float = 1.0) -> AadTape:
+    """10-asset equal-weight basket call, equicorrelation
+    0.5, 52 weekly steps, T = 1; 21 Greeks (10 spots, 10 vols, rate)."""
+    spots, vols = basket_config4_market(n, seed)
+    return AadRecorder.record(lambda rec: BasketOption.record(
+        rec, spots, vols, rate, [1.0 / n] * n, strike, equicorrelation(n, rho), maturity, steps))
+
+
 def record_model(market, product: Product, grid: TimeGrid) -> AadTape:
     """Nabla.model(market, (rec, in) -> product.record(rec, in, grid)).tape()."""
     def body(rec):

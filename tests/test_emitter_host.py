@@ -109,6 +109,14 @@ def test_fp32_host_build_tracks_the_fp32_oracle(oracle_mod):
     _run(oracle_mod, fp32_asian_50(50), [100.0, 0.2], 5_000, 0, 0xA51A17, rtol=2e-6, f32=True)
 
 
+@pytest.mark.parametrize("n,steps", [(3, 8), (4, 5)])
+def test_correlated_basket(oracle_mod, n, steps):
+    """BASELINE config 4's shape (Cholesky mix of n normals per step, n GBM
+    assets, 2n + 1 inputs) at a size the host runs quickly."""
+    tape = quant.basket_tape(n=n, steps=steps)
+    _run(oracle_mod, tape, tape.recordedInputs(), 2_000, 5, 7)
+
+
 def test_loop_plan_reported_for_config_tapes(ntlib):
     src = _lib.emit_source(quant.barrier_tape(252), target=0, precision=0)
     assert "step loop: 126 units of 32 nodes (2 steps each)" in src

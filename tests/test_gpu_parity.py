@@ -207,6 +207,17 @@ def test_general_tapes_fp64(engine, oracle_mod, make, inputs, seed):
     _assert_parity(got, want, scale)
 
 
+def test_basket_config4_fp64(engine, oracle_mod):
+    """10-asset basket, 52 weekly steps, 21 Greeks."""
+    tape = quant.basket_tape()
+    assert tape.input_count() == 21
+    with engine.compile(tape, FP64) as ex:
+        assert ex.info()["loop_units"] == 52
+        got, _ = ex.replay_sums(20_000, 0x1_0000_0003, 7)
+    want, scale = _oracle(oracle_mod, tape, tape.recordedInputs(), 20_000, 0x1_0000_0003, 7)
+    _assert_parity(got, want, scale)
+
+
 def test_replay_safe_matches_single_dispatch(engine):
     tape = quant.asian_tape(252)
     with engine.compile(tape, FP64) as ex:
