@@ -16,7 +16,9 @@ Prints one JSON line on rank 0.  `value` is whole-job scenarios/s timed with
 CUDA events on the engine's stream (inputs resident, max over ranks); `e2e`
 is the same metric through the C ABI with host inputs and a host read of the
 sums every step; `roofline` relates the replay kernel's algorithmic fp64
-flops to the measured DFMA peak; `cpu_baseline` is the CPU oracle (a port of
+flops to the measured DFMA peak (the rate held under the power limit when the
+timed region lasts seconds, with the burst figure beside it); `cpu_baseline`
+is the CPU oracle (a port of
 the reference's scalar `cpu` engine) on a bounded sample on this host.
 `--impl reference` times that CPU oracle alone on all host threads: the
 reference is Java and cannot run here (no JVM).
@@ -222,7 +224,6 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
         uid = [dist_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ex.distAttach(world, rank, uid[0], timeout_ms=120_000)
-    peak = _lib.fma_peak(local_rank, not wl.f32)
 
     total = int(args.paths if args.paths is not None else wl.paths)
     chunk = int(args.chunk if args.chunk is not None else wl.chunk)
@@ -274,13 +275,26 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
     e2e_value = args.steps * total / e2e_total
 
     # ---- roofline of the replay kernel ------------------------------------------
+    # Both peaks are measured after the timed region: the burst (short
+    # launches at boost clock) and the sustained rate (3 s of back-to-back
+    # launches under the 1 kW power limit).  A timed region longer than a
+    # second runs power-limited, so its denominator is the sustained figure.
+    peak_burst = _lib.fma_peak(local_rank, not wl.f32)
+    peak_sus = _lib.fma_peak_sustained(local_rank, not wl.f32, 3000)
+    long_run = my_total_ms > 1000.0
+    peak = peak_sus if long_run else peak_burst
     flops_per_scen = info["fwd_flops"] + info["rev_flops"]
     kernel_s = (my_total_ms * 1e-3) / (args.steps * launches_per_step)
     paths_per_launch = mine / launches_per_step
     achieved = flops_per_scen * paths_per_launch / kernel_s / 1e12
+    pipe = "FFMA" if wl.f32 else "DFMA"
     roofline = {"bound": wl.dtype.replace("f", "fp"), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak,
-                "peak_source": f"measured {'FFMA' if wl.f32 else 'DFMA'} peak on this GPU (nt_fma_peak, of measured)",
+                "peak_source": (f"measured {pipe} rate on this GPU, of measured: "
+                                + ("sustained over 3 s under the power limit (nt_fma_peak_sustained), the "
+                                   "timed region being longer than 1 s" if long_run else
+                                   "burst (nt_fma_peak), the timed region being shorter than 1 s")),
+                "peak_burst": peak_burst, "peak_sustained": peak_sus, "frac_of_burst": achieved / peak_burst,
                 "flops_per_scenario": flops_per_scen, "traffic": _profiled_traffic(wl, paths_per_launch)}
 
     line = None

@@ -298,13 +298,20 @@ int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t s
  * counterpart in the reference (it reports no roofline). */
 int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops);
 
+/* The same FMA chains launched back to back for `millis` milliseconds; the
+ * rate over the second half, once the clocks have settled under the board's
+ * power limit.  The denominator for a replay timed over seconds (a burst
+ * figure would credit clocks the long run cannot hold).  No counterpart in
+ * the reference. */
+int nt_fma_peak_sustained(int32_t device, int32_t fp64, int32_t millis, double* tflops);
+
 /* Launches one math-probe kernel (148*4 blocks of 256 threads, `iters` calls
  * each) for instruction / flop counting under ncu: which = 0 empty loop,
  * 1 library exp, 2 library log, 3 library sincos, 4 library sqrt, 5 the
  * replay's exp, 6 its series -2 ln(u1), 7 its series sincos(2 pi u2),
  * 8 library exp on a wide range, 9 the table-driven -2 ln(u1), 10 the
- * table-driven sincos(2 pi u2), 11 the radius sqrt.  No counterpart in the
- * reference. */
+ * table-driven sincos(2 pi u2), 11 the radius sqrt, 12 the Taylor-series
+ * exp, 13 one Philox2x32-10 block.  No counterpart in the reference. */
 int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 
 #ifdef __cplusplus

@@ -109,6 +109,7 @@ SIGNATURES = {
     "nt_philox_words": ([ctypes.c_int32, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32,
                          ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32), _f64p], ctypes.c_int),
     "nt_fma_peak": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
+    "nt_fma_peak_sustained": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
     "nt_math_probe": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
     "nt_replay_noalloc": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
                            ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
@@ -116,7 +117,8 @@ SIGNATURES = {
 
 MATH_PROBES = {0: "loop", 1: "exp(lib, |x|<=1/8)", 2: "log(lib)", 3: "sincos(lib)", 4: "sqrt(lib)",
                5: "exp(replay)", 6: "-2ln(u1)(series)", 7: "sincos(2pi u2)(series)", 8: "exp(lib, |x|<=4)",
-               9: "-2ln(u1)(table)", 10: "sincos(2pi u2)(table)", 11: "sqrt(replay radius)"}
+               9: "-2ln(u1)(table)", 10: "sincos(2pi u2)(table)", 11: "sqrt(replay radius)",
+               12: "exp(Taylor series)", 13: "philox2x32-10 block"}
 
 
 def math_probe(device: int, which: int, iters: int) -> float:
@@ -129,6 +131,14 @@ def fma_peak(device: int = 0, fp64: bool = True, iters: int = 4096) -> float:
     """Measured vector-FMA peak in TFLOP/s (nt_fma_peak)."""
     out = ctypes.c_double(0.0)
     check(lib().nt_fma_peak(device, int(fp64), iters, ctypes.byref(out)))
+    return out.value
+
+
+def fma_peak_sustained(device: int = 0, fp64: bool = True, millis: int = 3000) -> float:
+    """Vector-FMA rate held over `millis` of back-to-back launches, in
+    TFLOP/s (nt_fma_peak_sustained): the power-limited peak."""
+    out = ctypes.c_double(0.0)
+    check(lib().nt_fma_peak_sustained(device, int(fp64), millis, ctypes.byref(out)))
     return out.value
 
 

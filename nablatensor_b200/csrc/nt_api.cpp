@@ -234,7 +234,7 @@ extern "C" int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_of
 
 extern "C" int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum) {
   return guarded([&] {
-    if (which < 0 || which > 11) nt::fail(NT_E_INVALID_ARG, "which must be in [0, 11]");
+    if (which < 0 || which > 13) nt::fail(NT_E_INVALID_ARG, "which must be in [0, 13]");
     if (iters <= 0) nt::fail(NT_E_INVALID_ARG, "iters must be positive");
     nt::math_probe(device, which, iters, checksum);
   });
@@ -245,5 +245,13 @@ extern "C" int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* 
     if (!tflops) nt::fail(NT_E_INVALID_ARG, "tflops is null");
     if (iters <= 0) nt::fail(NT_E_INVALID_ARG, "iters must be positive");
     *tflops = nt::fma_peak_tflops(device, fp64, iters);
+  });
+}
+
+extern "C" int nt_fma_peak_sustained(int32_t device, int32_t fp64, int32_t millis, double* tflops) {
+  return guarded([&] {
+    if (!tflops) nt::fail(NT_E_INVALID_ARG, "tflops is null");
+    if (millis <= 0 || millis > 60000) nt::fail(NT_E_INVALID_ARG, "millis must be in [1, 60000]");
+    *tflops = nt::fma_peak_sustained_tflops(device, fp64, millis);
   });
 }

@@ -275,12 +275,27 @@ NT_FN double nt_sqrt_pos(double a) {
 #endif
 }
 
-/* EXP nodes of fp64 tapes: the dedicated routine on the device, libm in the
- * host build (bit-for-bit with the oracle). */
+#ifndef NT_HOST
+/* nt_exp64 with the warp's active lanes taken once per scenario by the
+ * caller (the replay kernel's scenario body has no divergent region around
+ * its EXP nodes), which saves the mask query at every node. */
+NT_FN double nt_exp64m(double x, unsigned lanes) {
+  double r = nt_exp_small(x);
+  const bool big = !(fabs(x) <= 0.125);
+  if (__any_sync(lanes, big)) {
+    if (big) r = exp(x);
+  }
+  return r;
+}
+#endif
+
+/* EXP nodes of fp64 tapes: the dedicated routine on the device (the emitted
+ * kernel declares nt_lanes = __activemask() at the top of each scenario),
+ * libm in the host build (bit-for-bit with the oracle). */
 #ifdef NT_HOST
 #define NT_EXP64(x) exp(x)
 #else
-#define NT_EXP64(x) nt_exp64(x)
+#define NT_EXP64(x) nt_exp64m((x), nt_lanes)
 #endif
 
 /* ---- table-driven Box-Muller ---------------------------------------------

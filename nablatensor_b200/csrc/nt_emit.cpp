@@ -21,6 +21,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <set>
 #include <sstream>
 
 #include "nt_internal.hpp"
@@ -74,6 +75,19 @@ class Emitter {
   const EmitConfig& cfg_;
   const bool acc_smem_;
   Out o_;
+  // Adjoint registers that still hold their initial zero at this point of the
+  // emitted straight-line code.  In fp64 the first contribution to one is
+  // emitted as an assignment: `0 + x` and `x` differ only in the sign of an
+  // exact zero, which no later adjoint rule can observe (adjoints are only
+  // scaled and summed, and every accumulator starts at +0).  fp32 keeps the
+  // explicit `0 + x`: the product then stays rounded on its own instead of
+  // being fused into the next addition, which is what the reference's
+  // node-by-node fp32 rounding needs.
+  std::set<std::string> zero_;
+  std::string contrib(const std::string& x, char sign, const std::string& e) {
+    if (zero_.erase(x) && !cfg_.f32) return x + " = " + (sign == '-' ? "-(" + e + ")" : e) + ";";
+    return x + (sign == '-' ? " -= " : " += ") + e + ";";
+  }
 
   std::string R(const char* f64, const char* f32) const { return cfg_.f32 ? f32 : f64; }
   std::string rng_pair() const {
@@ -141,42 +155,49 @@ void Emitter::emit_rule(int op, const std::string& D, const std::string& Va, con
   const std::string zero = cfg_.f32 ? "0.0f" : "0.0";
   switch (op) {
     case NT_ADD:
-      if (da) o_.line(*da + " += " + D + ";");
-      if (db) o_.line(*db + " += " + D + ";");
+      if (da) o_.line(contrib(*da, '+', D));
+      if (db) o_.line(contrib(*db, '+', D));
       break;
     case NT_SUB:
-      if (da) o_.line(*da + " += " + D + ";");
-      if (db) o_.line(*db + " -= " + D + ";");
+      if (da) o_.line(contrib(*da, '+', D));
+      if (db) o_.line(contrib(*db, '-', D));
       break;
     case NT_MUL:
-      if (da) o_.line(*da + " += " + D + " * " + Vb + ";");
-      if (db) o_.line(*db + " += " + D + " * " + Va + ";");
+      if (da) o_.line(contrib(*da, '+', D + " * " + Vb));
+      if (db) o_.line(contrib(*db, '+', D + " * " + Va));
       break;
     case NT_DIV:
-      if (da) o_.line(*da + " += " + D + " / " + Vb + ";");
-      if (db) o_.line(*db + " -= " + D + " * " + Vi + " / " + Vb + ";");
+      if (da) o_.line(contrib(*da, '+', D + " / " + Vb));
+      if (db) o_.line(contrib(*db, '-', D + " * " + Vi + " / " + Vb));
       break;
     case NT_NEG:
-      if (da) o_.line(*da + " -= " + D + ";");
+      if (da) o_.line(contrib(*da, '-', D));
       break;
     case NT_EXP:
-      if (da) o_.line(*da + " += " + D + " * " + Vi + ";");
+      if (da) o_.line(contrib(*da, '+', D + " * " + Vi));
       break;
     case NT_LOG:
-      if (da) o_.line(*da + " += " + D + " / " + Va + ";");
+      if (da) o_.line(contrib(*da, '+', D + " / " + Va));
       break;
     case NT_SQRT:
-      if (da) o_.line(*da + " += " + D + " * " + half + " / " + Vi + ";");
+      if (da) o_.line(contrib(*da, '+', D + " * " + half + " / " + Vi));
       break;
     case NT_ABS:
-      if (da) o_.line(*da + " += " + Va + " < " + zero + " ? -" + D + " : " + D + ";");
+      if (da) o_.line(contrib(*da, '+', "(" + Va + " < " + zero + " ? -" + D + " : " + D + ")"));
       break;
     case NT_MAX:
     case NT_MIN: {
+      // A branch that is not taken leaves its register as it was, so an
+      // assignment in the branch is still exact.
       const std::string cmp = "(" + Va + (op == NT_MAX ? " >= " : " <= ") + Vb + ")";
-      if (da && db) o_.line("if " + cmp + " " + *da + " += " + D + "; else " + *db + " += " + D + ";");
-      else if (da) o_.line("if " + cmp + " " + *da + " += " + D + ";");
-      else if (db) o_.line("if (!" + cmp + ") " + *db + " += " + D + ";");
+      if (da && db) {
+        const std::string sa = contrib(*da, '+', D), sb = contrib(*db, '+', D);
+        o_.line("if " + cmp + " " + sa + " else " + sb);
+      } else if (da) {
+        o_.line("if " + cmp + " " + contrib(*da, '+', D));
+      } else if (db) {
+        o_.line("if (!" + cmp + ") " + contrib(*db, '+', D));
+      }
       break;
     }
     default: break;
@@ -323,16 +344,21 @@ void Emitter::emit_body_reverse(int g) {
     return "d" + std::to_string(r.idx);
   };
   o_.open("{");
+  zero_.clear();  // the unit's own registers start at zero; outer ones never do here
   for (int32_t j = 0; j < L; ++j) {
     const BodyNode& bn = lp_.body[j];
     if (!bn.active) continue;
     std::string init = cfg_.f32 ? "0.0f" : "0.0";
     if (lp_.is_carry[j]) init = "cd" + std::to_string(j);
     else if (lp_.is_exit[j]) init = "xd" + std::to_string(j);
+    else zero_.insert("b" + std::to_string(j));
     o_.line("real b" + std::to_string(j) + " = " + init + ";");
   }
   for (int32_t k : lp_.carries)
-    if (lp_.body[k].active) o_.line("real n" + std::to_string(k) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+    if (lp_.body[k].active) {
+      o_.line("real n" + std::to_string(k) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+      zero_.insert("n" + std::to_string(k));
+    }
   for (int32_t j = L - 1; j >= 0; --j) {
     const BodyNode& bn = lp_.body[j];
     if (!bn.active || nargs(bn.op) == 0) continue;
@@ -347,6 +373,7 @@ void Emitter::emit_body_reverse(int g) {
     if (lp_.body[k].active) o_.line("cd" + std::to_string(k) + " = n" + std::to_string(k) + ";");
   for (int32_t j : lp_.exits)
     if (!lp_.is_carry[j] && lp_.body[j].active) o_.line("xd" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+  zero_.clear();
   o_.close();
 }
 
@@ -357,22 +384,34 @@ void Emitter::emit_reverse_for_output(int o) {
   const int32_t stride = 2 + t_.n_in();
   o_.open("{  // reverse sweep, output " + std::to_string(o));
   // Adjoint registers of every active node outside the loop.
+  zero_.clear();
   for (int32_t i = 0; i < t_.n; ++i) {
     if (in_loop(i) || !t_.active[i]) continue;
     o_.line("real d" + std::to_string(i) + " = " + zero + ";");
+    zero_.insert("d" + std::to_string(i));
   }
   if (lp_.present) {
     for (int32_t k : lp_.carries)
-      if (lp_.body[k].active) o_.line("real cd" + std::to_string(k) + " = " + zero + ";");
+      if (lp_.body[k].active) {
+        o_.line("real cd" + std::to_string(k) + " = " + zero + ";");
+        zero_.insert("cd" + std::to_string(k));
+      }
     for (int32_t j : lp_.exits)
-      if (!lp_.is_carry[j] && lp_.body[j].active) o_.line("real xd" + std::to_string(j) + " = " + zero + ";");
+      if (!lp_.is_carry[j] && lp_.body[j].active) {
+        o_.line("real xd" + std::to_string(j) + " = " + zero + ";");
+        zero_.insert("xd" + std::to_string(j));
+      }
   }
-  if (active_outside(out)) o_.line(adj_outside(out) + " = " + one + ";");
+  if (active_outside(out)) {
+    o_.line(adj_outside(out) + " = " + one + ";");
+    zero_.erase(adj_outside(out));
+  }
 
   if (!lp_.present) {
     emit_straight_reverse(0, t_.n);
   } else {
     emit_straight_reverse(lp_.end(), t_.n);
+    zero_.clear();  // the segment loop runs its code more than once
     const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
     const int32_t nck = (int32_t)lp_.ckpt.size();
     o_.open("for (int s = " + std::to_string(K - 1) + "; s >= 0; --s) {");
@@ -513,14 +552,21 @@ std::string Emitter::run() {
     return o_.s;
   }
   o_.line("#define NT_BLOCK " + std::to_string(cfg_.block));
+  // Global checkpoints and the value tape are laid out in one tile per block,
+  // value-major inside the tile: a warp's store or load of one value is 32
+  // consecutive words (one coalesced 256-byte transaction in fp64), and the
+  // distance between two values is the compile-time constant NT_BLOCK, so the
+  // unrolled segment code addresses them with immediate offsets.
+  const bool gck = cfg_.global_ckpt && lp_.present && !lp_.ckpt.empty();
+  const bool tape = lp_.present && lp_.n_tape > 0;
   if (cfg_.global_ckpt) {
-    o_.line("#define NT_CK(slot) nt_gck[(nt_u64)(slot) * nt_gthreads + nt_gtid]");
+    o_.line("#define NT_CKV " + std::to_string(lp_.present ? lp_.K * (int32_t)lp_.ckpt.size() : 0));
+    o_.line("#define NT_CK(slot) nt_gck_b[(slot) * NT_BLOCK]");
   } else {
     o_.line("#define NT_CK(slot) nt_ck[(slot) * NT_BLOCK + threadIdx.x]");
   }
-  // Per-thread value tape, unit-major so each warp's store or load of one
-  // slot is 32 consecutive values (one coalesced 256-byte transaction in fp64).
-  o_.line("#define NT_TAPE(u, slot) nt_tape[((nt_u64)(u) * NT_NTAPE + (slot)) * nt_gthreads + nt_gtid]");
+  o_.line("#define NT_NLOOP " + std::to_string(lp_.present ? lp_.N : 0));
+  o_.line("#define NT_TAPE(u, slot) nt_tape_b[((u) * NT_NTAPE + (slot)) * NT_BLOCK]");
   std::string bounds = "__launch_bounds__(NT_BLOCK" + (cfg_.min_blocks > 0 ? ", " + std::to_string(cfg_.min_blocks) : std::string()) + ")";
   o_.line("extern \"C\" __global__ void " + bounds + " nt_replay_kernel(");
   o_.line("    const double* __restrict__ inputs, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
@@ -532,6 +578,11 @@ std::string Emitter::run() {
   o_.line("const nt_u64 nt_gtid = (nt_u64)blockIdx.x * NT_BLOCK + threadIdx.x;");
   o_.line("const nt_u64 nt_gthreads = (nt_u64)gridDim.x * NT_BLOCK;");
   o_.line("(void)nt_gck; (void)nt_gthreads; (void)nt_tape;");
+  if (gck)
+    o_.line("real* __restrict__ const nt_gck_b = nt_gck + (nt_u64)blockIdx.x * (NT_CKV * NT_BLOCK) + threadIdx.x;");
+  if (tape)
+    o_.line("real* __restrict__ const nt_tape_b = nt_tape + (nt_u64)blockIdx.x * ((nt_u64)NT_NLOOP * NT_NTAPE * "
+            "NT_BLOCK) + threadIdx.x;");
   for (int32_t j = 0; j < t_.n_in(); ++j)
     o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
   if (acc_smem_) {
@@ -550,6 +601,8 @@ std::string Emitter::run() {
   o_.line("nt_math_tables_load();");
   o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
   o_.line("const nt_u64 path = p + path_offset;");
+  o_.line("const unsigned nt_lanes = __activemask();");
+  o_.line("(void)nt_lanes;");
   emit_scenario();
   o_.close();
   if (acc_smem_) {

@@ -187,9 +187,8 @@ void Exec::load(int max_regs) {
   cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
   if (prop.major != 10) fail(NT_E_UNSUPPORTED, std::string("this engine targets sm_100 (B200); device is ") + prop.name);
   sm_count = prop.multiProcessorCount;
-  (void)max_regs;
   double secs = 0.0;
-  std::vector<char> cubin = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs, cfg.fmad);
+  std::vector<char> cubin = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs, cfg.fmad, max_regs);
   const auto t0 = std::chrono::steady_clock::now();
   Driver& d = driver();
   cu_check(d.moduleLoadData(&module, cubin.data()), "cuModuleLoadData");

@@ -134,15 +134,19 @@ extern const double kFlopWeights[4];
 // Math probe launches (per-call counts under ncu).
 void math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 
-// Vector-FMA peak (TFLOP/s) measured with independent FMA chains.
+// Vector-FMA peak (TFLOP/s) measured with independent FMA chains: a burst
+// (best of a few short launches) and a sustained rate (launches back to back
+// for `millis`, rate over the second half, under the board's power limit).
 double fma_peak_tflops(int32_t device, int32_t fp64, int32_t iters);
+double fma_peak_sustained_tflops(int32_t device, int32_t fp64, int32_t millis);
 
 // Runs the device Philox/Box-Muller for the known-answer interface.
 void philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t seed, int32_t stream,
                   uint32_t pair0, uint32_t n_pairs, uint32_t* out, double* normals);
 
-// NVRTC: compile to an sm_100a cubin (cached in memory and on disk).
+// NVRTC: compile to an sm_100a cubin (cached in memory and on disk);
+// max_regs > 0 caps the registers per thread (--maxrregcount).
 std::vector<char> nvrtc_compile(const std::string& source, const std::string& arch, bool use_disk_cache,
-                                double* seconds, bool fmad = true);
+                                double* seconds, bool fmad = true, int max_regs = 0);
 
 }  // namespace nt

@@ -3,6 +3,7 @@
 // Exposes the raw Philox2x32-10 words and fp64 Box-Muller legs that every
 // replay kernel draws, so the tests can compare them with the oracle's
 // restatement of Philox.java bit for bit.
+#include <vector>
 #include "nt_device_rt.cuh"
 #include "nt_exec.hpp"
 
@@ -88,6 +89,7 @@ __global__ void __launch_bounds__(256) math_probe_kernel(int which, int iters, d
   nt_math_tables_load();
   const unsigned tid = blockIdx.x * blockDim.x + threadIdx.x;
   double acc = 0.0, acc2 = 0.0;
+  unsigned bits = 0;
   for (int i = 0; i < iters; ++i) {
     const unsigned w = probe_word(tid * 2654435761u + (unsigned)i);
     const double u = ((double)w + 0.5) * NT_UINT_SCALE;
@@ -105,10 +107,17 @@ __global__ void __launch_bounds__(256) math_probe_kernel(int which, int iters, d
       case 9: acc += nt_neg2log_u1_t(w); break;                       // table-driven -2 ln u1
       case 10: nt_sincos_2pi_u2_t(w, &s, &c); acc += s; acc2 += c; break;  // table-driven sincos
       case 11: acc += nt_sqrt_pos(u * 46.0); break;                   // the replay's radius sqrt
+      case 12: acc += nt_exp_small((u - 0.5) * 0.25); break;          // Taylor-series exp
+      case 13: {                                                       // one Philox block
+        nt_u32 a, b;
+        nt_philox(w, (unsigned)i, &a, &b);
+        bits ^= a ^ b;
+        break;
+      }
       default: break;
     }
   }
-  out[tid] = acc + acc2;
+  out[tid] = acc + acc2 + (double)bits;
 }
 
 }  // namespace
@@ -196,6 +205,53 @@ double fma_peak_tflops(int32_t device, int32_t fp64, int32_t iters) {
   cudaStreamDestroy(s);
   const double flops = 2.0 * 8 * 16 * (double)iters * blocks * 256;
   return flops / (best_ms * 1e-3) / 1e12;
+}
+
+double fma_peak_sustained_tflops(int32_t device, int32_t fp64, int32_t millis) {
+  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop;
+  cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  int per_sm = 0;
+  if (fp64)
+    cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fma_peak_kernel<double>, 256, 0), "occupancy");
+  else
+    cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fma_peak_kernel<float>, 256, 0), "occupancy");
+  const int blocks = prop.multiProcessorCount * per_sm;
+  const int iters = 4096;  // about 10 ms per launch
+  void* out = nullptr;
+  cudaStream_t s = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaMalloc(&out, (size_t)blocks * 256 * 8), "cudaMalloc");
+  cuda_check(cudaEventCreate(&e0), "cudaEventCreate");
+  cuda_check(cudaEventCreate(&e1), "cudaEventCreate");
+  // Launch back to back for `millis`; the rate is taken over the second half,
+  // once the clocks have settled under the board's power limit.
+  std::vector<float> ms_list;
+  double elapsed = 0.0;
+  while (elapsed < millis) {
+    cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
+    for (int k = 0; k < 8; ++k) {
+      if (fp64) fma_peak_kernel<double><<<blocks, 256, 0, s>>>((double*)out, iters, 0.999999, 1e-7);
+      else fma_peak_kernel<float><<<blocks, 256, 0, s>>>((float*)out, iters, 0.999999f, 1e-7f);
+    }
+    cuda_check(cudaGetLastError(), "fma_peak_kernel");
+    cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
+    cuda_check(cudaEventSynchronize(e1), "fma_peak_kernel");
+    float ms = 0;
+    cuda_check(cudaEventElapsedTime(&ms, e0, e1), "cudaEventElapsedTime");
+    ms_list.push_back(ms);
+    elapsed += ms;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaFree(out);
+  cudaStreamDestroy(s);
+  double tail_ms = 0.0;
+  size_t n = 0;
+  for (size_t i = ms_list.size() / 2; i < ms_list.size(); ++i, ++n) tail_ms += ms_list[i];
+  const double flops = 2.0 * 8 * 16 * (double)iters * blocks * 256 * 8 * (double)n;
+  return flops / (tail_ms * 1e-3) / 1e12;
 }
 
 }  // namespace nt

@@ -60,7 +60,7 @@ void check(nvrtcResult r, const char* what) {
 }  // namespace
 
 std::vector<char> nvrtc_compile(const std::string& source, const std::string& arch, bool use_disk_cache,
-                                double* seconds, bool fmad) {
+                                double* seconds, bool fmad, int max_regs) {
   int major = 0, minor = 0;
   nvrtcVersion(&major, &minor);
   std::vector<std::string> opts = {
@@ -71,6 +71,7 @@ std::vector<char> nvrtc_compile(const std::string& source, const std::string& ar
       "--extra-device-vectorization",
       "-lineinfo",
   };
+  if (max_regs > 0) opts.push_back("--maxrregcount=" + std::to_string(max_regs));
   std::string key_text = source + "\x01" + kDeviceRuntimeSource + "\x01" + kMathTablesSource + "\x01" +
                          std::to_string(major) + "." + std::to_string(minor);
   for (auto& o : opts) key_text += "\x02" + o;

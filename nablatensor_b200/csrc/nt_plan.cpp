@@ -286,6 +286,8 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   if (cfg.block % 32 != 0 || cfg.block > 1024) fail(NT_E_INVALID_ARG, "block must be a multiple of 32, <= 1024");
   if (opt->min_blocks < 0 || opt->min_blocks > 32) fail(NT_E_INVALID_ARG, "min_blocks must be in [0, 32]");
   if (opt->seg_units < 0) fail(NT_E_INVALID_ARG, "seg_units must be >= 0");
+  if (opt->max_regs != 0 && (opt->max_regs < 32 || opt->max_regs > 255))
+    fail(NT_E_INVALID_ARG, "max_regs must be 0 or in [32, 255]");
   cfg.min_blocks = opt->min_blocks;
   cfg.seg_units = opt->seg_units;
   cfg.target = target;

@@ -95,6 +95,10 @@ def test_invalid_arguments(ntlib):
     with pytest.raises(_lib.NablaError) as e:
         _lib.emit_source(quant.asian_tape(4), target=2)
     assert e.value.code == _lib.NT_E_INVALID_ARG
+    for regs in (8, 256, -1):
+        with pytest.raises(_lib.NablaError) as e:
+            _lib.emit_source(quant.asian_tape(4), max_regs=regs)
+        assert e.value.code == _lib.NT_E_INVALID_ARG and "max_regs" in str(e.value)
 
 
 def test_bad_block_size_is_an_argument_error(ntlib):
