@@ -501,6 +501,17 @@ NT_FN void nt_prefetch_l2(const void* p) {
 #endif
 }
 
+/* Hint `bytes` bytes from p into L2 as one bulk request (p 16-byte aligned,
+ * bytes a multiple of 16): one thread covers a whole contiguous tile. */
+NT_FN void nt_prefetch_l2_bulk(const void* p, unsigned bytes) {
+#ifdef NT_HOST
+  (void)p;
+  (void)bytes;
+#else
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+#endif
+}
+
 /* ---- java.lang.Math semantics ------------------------------------------- */
 
 NT_FN bool nt_signbit64(double x) {

@@ -419,15 +419,16 @@ void Emitter::emit_reverse_for_output(int o) {
       o_.line("const real cs" + std::to_string(lp_.ckpt[c]) + " = NT_CK(s * " + std::to_string(nck) + " + " +
               std::to_string(c) + ");");
     if (lp_.n_tape > 0 && cfg_.target == 0) {
-      // The previous segment's tape lines head for L2 while this one is reversed.
-      o_.open("if (s > 0) {");
-      for (int g = 0; g < G; ++g)
-        for (int32_t k = 0; k < lp_.n_tape; ++k)
-          o_.line("nt_prefetch_l2(&NT_TAPE((s - 1) * " + std::to_string(G) + " + " + std::to_string(g) + ", " +
-                  std::to_string(k) + "));");
-      if (cfg_.global_ckpt)
-        for (int32_t c = 0; c < nck; ++c)
-          o_.line("nt_prefetch_l2(&NT_CK((s - 1) * " + std::to_string(nck) + " + " + std::to_string(c) + "));");
+      // The previous segment's tape (and checkpoint) rows of the whole block
+      // are one contiguous range of the block's tile: one thread sends them
+      // to L2 as a bulk prefetch while this segment is reversed.
+      const std::string seg = std::to_string(G) + " * NT_NTAPE * NT_BLOCK";
+      o_.open("if (s > 0 && threadIdx.x == 0) {");
+      o_.line("nt_prefetch_l2_bulk(nt_tape_blk + (nt_u64)(s - 1) * (" + seg + "), (unsigned)(" + seg +
+              " * sizeof(real)));");
+      if (cfg_.global_ckpt && nck > 0)
+        o_.line("nt_prefetch_l2_bulk(nt_gck_blk + (nt_u64)(s - 1) * (" + std::to_string(nck) +
+                " * NT_BLOCK), (unsigned)(" + std::to_string(nck) + " * NT_BLOCK * sizeof(real)));");
       o_.close();
     }
     for (int g = 0; g < G; ++g) {
@@ -578,11 +579,15 @@ std::string Emitter::run() {
   o_.line("const nt_u64 nt_gtid = (nt_u64)blockIdx.x * NT_BLOCK + threadIdx.x;");
   o_.line("const nt_u64 nt_gthreads = (nt_u64)gridDim.x * NT_BLOCK;");
   o_.line("(void)nt_gck; (void)nt_gthreads; (void)nt_tape;");
-  if (gck)
-    o_.line("real* __restrict__ const nt_gck_b = nt_gck + (nt_u64)blockIdx.x * (NT_CKV * NT_BLOCK) + threadIdx.x;");
-  if (tape)
-    o_.line("real* __restrict__ const nt_tape_b = nt_tape + (nt_u64)blockIdx.x * ((nt_u64)NT_NLOOP * NT_NTAPE * "
-            "NT_BLOCK) + threadIdx.x;");
+  if (gck) {
+    o_.line("real* __restrict__ const nt_gck_blk = nt_gck + (nt_u64)blockIdx.x * (NT_CKV * NT_BLOCK);");
+    o_.line("real* __restrict__ const nt_gck_b = nt_gck_blk + threadIdx.x;");
+  }
+  if (tape) {
+    o_.line("real* __restrict__ const nt_tape_blk = nt_tape + (nt_u64)blockIdx.x * ((nt_u64)NT_NLOOP * NT_NTAPE * "
+            "NT_BLOCK);");
+    o_.line("real* __restrict__ const nt_tape_b = nt_tape_blk + threadIdx.x;");
+  }
   for (int32_t j = 0; j < t_.n_in(); ++j)
     o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
   if (acc_smem_) {
