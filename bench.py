@@ -339,6 +339,10 @@ def _profiled_traffic(wl: Workload, paths_per_launch: float):
 
 
 def main():
+    # NCCL prints a version banner on stdout when a communicator is set up
+    # (NCCL_DEBUG unset or VERSION); stdout carries exactly one JSON line.
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
