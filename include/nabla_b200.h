@@ -86,8 +86,13 @@ typedef struct nt_tape {
 #define NT_FLAG_RECOMPUTE_ALL 0x40 /* reverse sweep recomputes every loop value from the step
                                       checkpoints (no per-thread value tape in global memory) */
 #define NT_FLAG_TAPE_DRAWS 0x80    /* tape only the draws and recompute exp/log/sqrt/div in the
-                                      reverse sweep (half the tape traffic); by default every
-                                      expensive loop value is taped */
+                                      reverse sweep.  By default the draws, log, sqrt, division
+                                      and every exp whose argument depends on a loop carry are
+                                      taped; an exp of the unit's draws and invariants alone (a
+                                      GBM log-return) is recomputed by the branch-free series,
+                                      unless the unit's reverse values alone need more than 32
+                                      registers */
+#define NT_FLAG_TAPE_ALL 0x100     /* tape every draw, exp, log, sqrt and division */
 
 /*
  * Compile options: AadOptions (AadOptions.java:42-156) plus the engine knobs a
@@ -132,6 +137,8 @@ typedef struct nt_exec_info {
   int32_t ckpt_global;      /* 1 when checkpoints live in global memory */
   int32_t tape_slots;       /* values per loop unit written to the per-thread tape (0: recompute all) */
   int32_t tape_mbytes;      /* device memory held by the value tape, MiB */
+  int32_t markets_registers;   /* the multi-market kernel's, 0 until nt_replay_markets compiled it */
+  int32_t markets_local_bytes;
   double compile_seconds;   /* NVRTC + module load, 0 on a cache hit */
   double fwd_flops;         /* algorithmic flops per scenario, forward (weights in DESIGN) */
   double rev_flops;         /* algorithmic flops per scenario, reverse */
@@ -174,6 +181,26 @@ int nt_replay(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed
               double* seconds);
 
 /*
+ * Re-pricing under several markets in one dispatch, with common random
+ * numbers: inputs holds n_states input vectors ([n_states][n_in], input
+ * order), sums receives n_states blocks in nt_replay's layout
+ * ([n_states][n_out * (2 + n_in)]).  Every scenario is replayed under each
+ * market in turn; the first market draws the step loop's normals and tapes
+ * them, the others read them back, so the generator and the Box-Muller
+ * transform run once per scenario instead of once per market.  Each
+ * market's sums equal nt_replay with those inputs up to the
+ * rounding of a multiply-add the compiler fuses differently in the two
+ * kernels (bit for bit in the host build, which fuses none).  The executable's own
+ * inputs (nt_set_inputs) are not used or changed.  The kernel is compiled on
+ * the first call.  Replaces the per-market loop of
+ * ScenarioRunner.run/ladder (nablatensor-quant/.../scenario/ScenarioRunner.java:36-71),
+ * and the draw cache of the cpu-jit engine, CategoryEnum.DRAW_CACHE
+ * (nablatensor-engine-cpu/.../jit/JitReplay.java:69-89).
+ */
+int nt_replay_markets(nt_exec* exec, int32_t n_states, const double* inputs, uint64_t paths, uint64_t path_offset,
+                      uint64_t seed, double* sums, double* seconds);
+
+/*
  * Device-resident accumulation for long runs (the many-chunk replaySafe of
  * AbstractAadExecutable.java:101-121 without a read-back per chunk):
  * nt_replay_accumulate enqueues one dispatch that ADDS its sums into the
@@ -202,7 +229,13 @@ int nt_exec_source(nt_exec* exec, char* buf, size_t cap, size_t* len);
  *                                  uint64_t path_offset, uint64_t seed,
  *                                  double* sums)
  *   entry point (paths in order, sums in nt_replay's layout); it includes
- *   nt_device_rt.cuh and must be compiled with -DNT_HOST.
+ *   nt_device_rt.cuh and must be compiled with -DNT_HOST;
+ * target 2: the CUDA C of the multi-market kernel nt_replay_markets runs;
+ * target 3: its host C++, entry point
+ *   extern "C" void nt_host_replay_markets(const double* inputs, int n_states,
+ *                                          uint64_t paths, uint64_t path_offset,
+ *                                          uint64_t seed, double* sums)
+ *   (inputs [n_states][n_in], sums [n_states][channels]).
  */
 int nt_emit_source(const nt_tape* tape, const nt_options* options, int32_t target, char* buf,
                    size_t cap, size_t* len);

@@ -36,6 +36,7 @@ NT_FLAG_NO_FMAD = 0x10
 NT_FLAG_ACC_REGS = 0x20
 NT_FLAG_RECOMPUTE_ALL = 0x40
 NT_FLAG_TAPE_DRAWS = 0x80
+NT_FLAG_TAPE_ALL = 0x100
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _f64p = ctypes.POINTER(ctypes.c_double)
@@ -59,7 +60,8 @@ class NtExecInfo(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in (
         "registers", "local_bytes", "static_smem", "dynamic_smem", "block", "blocks_per_sm", "grid", "sm_count",
         "channels", "loop_start", "loop_unit", "loop_units", "steps_per_unit", "seg_units", "segments",
-        "ckpt_slots", "stored_per_unit", "ckpt_global", "tape_slots", "tape_mbytes")] + [
+        "ckpt_slots", "stored_per_unit", "ckpt_global", "tape_slots", "tape_mbytes", "markets_registers",
+        "markets_local_bytes")] + [
         ("compile_seconds", ctypes.c_double), ("fwd_flops", ctypes.c_double), ("rev_flops", ctypes.c_double)]
 
     def as_dict(self) -> dict:
@@ -86,6 +88,8 @@ SIGNATURES = {
     "nt_compile": ([ctypes.POINTER(NtTape), ctypes.POINTER(NtOptions), ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "nt_set_inputs": ([ctypes.c_void_p, _f64p, ctypes.c_int32], ctypes.c_int),
     "nt_replay": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _f64p, _f64p], ctypes.c_int),
+    "nt_replay_markets": ([ctypes.c_void_p, ctypes.c_int32, _f64p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
+                           _f64p, _f64p], ctypes.c_int),
     "nt_replay_accumulate": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
     "nt_accumulator_read": ([ctypes.c_void_p, _f64p, ctypes.c_int32], ctypes.c_int),
     "nt_exec_stream": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),

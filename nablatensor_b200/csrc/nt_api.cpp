@@ -102,6 +102,15 @@ int nt_replay(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed
   });
 }
 
+int nt_replay_markets(nt_exec* exec, int32_t n_states, const double* inputs, uint64_t paths, uint64_t path_offset,
+                      uint64_t seed, double* sums, double* seconds) {
+  return guarded([&] {
+    nt::Exec& x = impl(exec);
+    std::lock_guard<std::mutex> lk(x.mu);
+    x.markets(n_states, inputs, paths, path_offset, seed, sums, seconds);
+  });
+}
+
 int nt_replay_accumulate(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed) {
   return guarded([&] {
     nt::Exec& x = impl(exec);

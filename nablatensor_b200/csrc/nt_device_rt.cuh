@@ -289,13 +289,38 @@ NT_FN double nt_exp64m(double x, unsigned lanes) {
 }
 #endif
 
+#ifndef NT_HOST
+/* nt_exp64m that also records in `wide` whether this lane's argument left the
+ * series range.  A scenario whose forward sweep never did (for any lane of the
+ * warp) recomputes its exps in the reverse sweep with the bare series: the
+ * recomputed arguments are the forward's, so the result is the same, and the
+ * segment's exps, free of branches, interleave. */
+NT_FN double nt_exp64w(double x, unsigned lanes, bool& wide) {
+  double r = nt_exp_small(x);
+  const bool big = !(fabs(x) <= 0.125);
+  wide |= big;
+  if (__any_sync(lanes, big)) {
+    if (big) r = exp(x);
+  }
+  return r;
+}
+#endif
+
 /* EXP nodes of fp64 tapes: the dedicated routine on the device (the emitted
- * kernel declares nt_lanes = __activemask() at the top of each scenario),
- * libm in the host build (bit-for-bit with the oracle). */
+ * kernel declares nt_lanes = __activemask() and nt_wide at the top of each
+ * scenario), libm in the host build (bit-for-bit with the oracle).
+ * NT_EXP64W is the forward sweep's form for a loop exp the reverse sweep
+ * recomputes (it records wide arguments in nt_wide); NT_EXP64_SERIES is that
+ * recompute once the forward sweep has shown every argument of the warp in the
+ * series range. */
 #ifdef NT_HOST
 #define NT_EXP64(x) exp(x)
+#define NT_EXP64W(x) exp(x)
+#define NT_EXP64_SERIES(x) exp(x)
 #else
 #define NT_EXP64(x) nt_exp64m((x), nt_lanes)
+#define NT_EXP64W(x) nt_exp64w((x), nt_lanes, nt_wide)
+#define NT_EXP64_SERIES(x) nt_exp_small(x)
 #endif
 
 /* ---- table-driven Box-Muller ---------------------------------------------
@@ -600,6 +625,48 @@ NT_FN void nt_grid_reduce(const double* acc, int channels, double* scratch, doub
     double s = 0.0;
     for (int w = 0; w < warps; ++w) s += scratch[c * warps + w];
     partials[(nt_u64)blockIdx.x * channels + c] = s;
+  }
+  __shared__ unsigned int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+      double s = 0.0;
+      for (unsigned int b = 0; b < gridDim.x; ++b) s += __ldcg(&partials[(nt_u64)b * channels + c]);
+      out[c] = accumulate ? out[c] + s : s;
+    }
+    if (threadIdx.x == 0) *ticket = 0u;
+  }
+}
+
+/* nt_grid_reduce for per-thread compensated sums kept in a block tile (the
+ * multi-market kernel, whose channel count is a launch argument): channel k
+ * of this thread is col[2k * stride] + col[(2k + 1) * stride].  Channels pass
+ * through the block `chunk` at a time (scratch holds chunk * warps doubles);
+ * the block records and the last-block sum are as in nt_grid_reduce, so the
+ * result is the same block-order sum. */
+NT_FN void nt_grid_reduce_cols(const double* col, int stride, int channels, int chunk, double* scratch,
+                               double* partials, unsigned int* ticket, double* out, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  for (int c0 = 0; c0 < channels; c0 += chunk) {
+    const int n = channels - c0 < chunk ? channels - c0 : chunk;
+    for (int c = 0; c < n; ++c) {
+      const int k = c0 + c;
+      double v = nt_warp_sum(col[(nt_u64)(2 * k) * stride] + col[(nt_u64)(2 * k + 1) * stride]);
+      if (lane == 0) scratch[c * warps + warp] = v;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+      double s = 0.0;
+      for (int w = 0; w < warps; ++w) s += scratch[c * warps + w];
+      partials[(nt_u64)blockIdx.x * channels + c0 + c] = s;
+    }
+    __syncthreads();
   }
   __shared__ unsigned int last;
   __threadfence();

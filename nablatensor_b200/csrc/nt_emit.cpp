@@ -84,6 +84,14 @@ class Emitter {
   // being fused into the next addition, which is what the reference's
   // node-by-node fp32 rounding needs.
   std::set<std::string> zero_;
+  // Multi-market kernel, states after the first: loop draws come back from
+  // the value tape instead of the generator.
+  bool reuse_draws_ = false;
+  // Reverse-sweep copy for warps whose forward exps all stayed in the series
+  // range: recomputed EXP nodes use the bare series (no per-node branch).
+  bool series_exp_ = false;
+  // The fp64 exp form fwd_expr emits (NT_EXP64, NT_EXP64W or NT_EXP64_SERIES).
+  std::string exp_fn_ = "NT_EXP64(";
   std::string contrib(const std::string& x, char sign, const std::string& e) {
     if (zero_.erase(x) && !cfg_.f32) return x + " = " + (sign == '-' ? "-(" + e + ")" : e) + ";";
     return x + (sign == '-' ? " -= " : " += ") + e + ";";
@@ -137,7 +145,10 @@ std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B
     case NT_MUL: return A + " * " + B;
     case NT_DIV: return A + " / " + B;
     case NT_NEG: return "-" + A;
-    case NT_EXP: return cfg_.wide32 ? "((float)NT_EXP64((double)" + A + "))" : R("NT_EXP64(", "expf(") + A + ")";
+    case NT_EXP: {
+      const std::string e = exp_fn_;
+      return cfg_.wide32 ? "((float)" + e + "(double)" + A + "))" : R(e.c_str(), "expf(") + A + ")";
+    }
     case NT_LOG: return cfg_.wide32 ? "((float)log((double)" + A + "))" : R("log(", "logf(") + A + ")";
     case NT_SQRT: return R("sqrt(", "sqrtf(") + A + ")";
     case NT_ABS: return R("fabs(", "fabsf(") + A + ")";
@@ -290,7 +301,7 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     if (recompute && !lp_.recompute[j]) continue;
     if (emitted[j]) continue;
     const BodyNode& bn = lp_.body[j];
-    if (recompute && lp_.tape_slot[j] >= 0) {
+    if (lp_.tape_slot[j] >= 0 && (recompute || (reuse_draws_ && is_draw(bn.op)))) {
       o_.line(name(j) + " = NT_TAPE(" + unit + ", " + std::to_string(lp_.tape_slot[j]) + ");");
       emitted[j] = 1;
       continue;
@@ -320,7 +331,12 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     }
     const std::string A = nargs(bn.op) >= 1 ? ref(bn.ra) : "";
     const std::string B = nargs(bn.op) >= 2 ? ref(bn.rb) : "";
+    // Loop exps the reverse sweep recomputes record wide arguments in the
+    // forward sweep; the recompute itself takes the series when none was.
+    if (recompute) exp_fn_ = series_exp_ ? "NT_EXP64_SERIES(" : "NT_EXP64(";
+    else if (lp_.recompute[j] && lp_.tape_slot[j] < 0) exp_fn_ = "NT_EXP64W(";
     o_.line(name(j) + " = " + fwd_expr(bn.op, A, B, bn.c, -1) + ";");
+    exp_fn_ = "NT_EXP64(";
     emitted[j] = 1;
   }
 }
@@ -462,12 +478,15 @@ void Emitter::emit_reverse_for_output(int o) {
 // running sum in the host target, which reproduces AadTotals.add exactly.
 void Emitter::acc_line(int32_t k, const std::string& x) {
   const std::string K = std::to_string(k);
-  if (cfg_.target == 1) o_.line("nt_acc[" + K + "] += " + x + ";");
+  if (cfg_.target == 1 && cfg_.markets) o_.line("nt_acc[nt_m * NT_CH + " + K + "] += " + x + ";");
+  else if (cfg_.target == 1) o_.line("nt_acc[" + K + "] += " + x + ";");
+  else if (cfg_.markets) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
   else if (acc_smem_) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
   else o_.line("nt_two_sum(&nt_acc[" + K + "], &nt_cmp[" + K + "], " + x + ");");
 }
 
 void Emitter::emit_scenario() {
+  if (cfg_.target == 0) o_.line("bool nt_wide = false;  // some EXP argument left the series range");
   // Stream keys.
   std::vector<uint8_t> used(t_.n_streams, 0);
   for (int32_t i = 0; i < t_.n; ++i)
@@ -488,24 +507,54 @@ void Emitter::emit_scenario() {
     for (int32_t j : lp_.exits)
       if (!lp_.is_carry[j]) o_.line("real xv" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
     const int32_t nck = (int32_t)lp_.ckpt.size();
-    o_.open("for (int s = 0; s < " + std::to_string(K) + "; ++s) {");
-    for (int32_t c = 0; c < nck; ++c)
-      o_.line("NT_CK(s * " + std::to_string(nck) + " + " + std::to_string(c) + ") = cv" + std::to_string(lp_.ckpt[c]) + ";");
-    if (cfg_.target == 0) o_.line("#pragma unroll " + std::to_string(std::max(1, cfg_.fwd_unroll)));
-    o_.open("for (int g = 0; g < " + std::to_string(G) + "; ++g) {");
-    o_.line("const int u = s * " + std::to_string(G) + " + g;");
-    std::string decl;
-    for (int32_t j = 0; j < L; ++j) decl += (j ? ", f" : "real f") + std::to_string(j);
-    o_.line(decl + ";");
-    emit_body_forward("f", "u", false, 0);
-    for (int32_t j = 0; j < L; ++j)
-      if (lp_.tape_slot[j] >= 0)
-        o_.line("NT_TAPE(u, " + std::to_string(lp_.tape_slot[j]) + ") = f" + std::to_string(j) + ";");
-    for (int32_t k : lp_.carries) o_.line("cv" + std::to_string(k) + " = f" + std::to_string(k) + ";");
-    for (int32_t j : lp_.exits)
-      if (!lp_.is_carry[j]) o_.line("xv" + std::to_string(j) + " = f" + std::to_string(j) + ";");
-    o_.close();
-    o_.close();
+    auto forward_loop = [&]() {
+      o_.open("for (int s = 0; s < " + std::to_string(K) + "; ++s) {");
+      for (int32_t c = 0; c < nck; ++c)
+        o_.line("NT_CK(s * " + std::to_string(nck) + " + " + std::to_string(c) + ") = cv" +
+                std::to_string(lp_.ckpt[c]) + ";");
+      if (reuse_draws_ && cfg_.target == 0) {
+        // The forward now reads the tape: the next segment's rows head for L2
+        // while this one runs, as in the reverse sweep.
+        const std::string seg = std::to_string(G) + " * NT_NTAPE * NT_BLOCK";
+        o_.line("if (s + 1 < " + std::to_string(K) + " && threadIdx.x == 0) nt_prefetch_l2_bulk(nt_tape_blk + "
+                "(nt_u64)(s + 1) * (" + seg + "), (unsigned)(" + seg + " * sizeof(real)));");
+      }
+      // A market that reads its draws back unrolls the segment, so the
+      // segment's tape loads are all in flight before the first unit needs
+      // one; the drawing loop stays rolled (it only stores).
+      if (cfg_.target == 0)
+        o_.line(reuse_draws_ ? std::string("#pragma unroll")
+                             : "#pragma unroll " + std::to_string(std::max(1, cfg_.fwd_unroll)));
+      o_.open("for (int g = 0; g < " + std::to_string(G) + "; ++g) {");
+      o_.line("const int u = s * " + std::to_string(G) + " + g;");
+      std::string decl;
+      for (int32_t j = 0; j < L; ++j) decl += (j ? ", f" : "real f") + std::to_string(j);
+      o_.line(decl + ";");
+      emit_body_forward("f", "u", false, 0);
+      for (int32_t j = 0; j < L; ++j)
+        if (lp_.tape_slot[j] >= 0 && !(reuse_draws_ && is_draw(lp_.body[j].op)))
+          o_.line("NT_TAPE(u, " + std::to_string(lp_.tape_slot[j]) + ") = f" + std::to_string(j) + ";");
+      for (int32_t k : lp_.carries) o_.line("cv" + std::to_string(k) + " = f" + std::to_string(k) + ";");
+      for (int32_t j : lp_.exits)
+        if (!lp_.is_carry[j]) o_.line("xv" + std::to_string(j) + " = f" + std::to_string(j) + ";");
+      o_.close();
+      o_.close();
+    };
+    bool taped_draws = false;
+    for (int32_t j = 0; j < L; ++j) taped_draws |= is_draw(lp_.body[j].op) && lp_.tape_slot[j] >= 0;
+    if (cfg_.markets && taped_draws) {
+      // The first market draws and tapes them; the others read them back.
+      o_.open("if (nt_m == 0) {");
+      forward_loop();
+      o_.close("} else {");
+      ++o_.ind;
+      reuse_draws_ = true;
+      forward_loop();
+      reuse_draws_ = false;
+      o_.close();
+    } else {
+      forward_loop();
+    }
     emit_straight_forward(lp_.end(), t_.n);
   }
   const int32_t stride = 2 + t_.n_in();
@@ -514,12 +563,33 @@ void Emitter::emit_scenario() {
     acc_line(o * stride, y);
     acc_line(o * stride + 1, y + " * " + y);
   }
-  if (cfg_.adjoints)
-    for (int32_t o = 0; o < t_.n_out(); ++o) emit_reverse_for_output(o);
+  if (cfg_.adjoints) {
+    // The reverse sweep recomputes EXP nodes when they are not taped
+    // (draws-only tape, recompute-all).  On the device it is emitted twice:
+    // the copy for warps whose forward exps all stayed in the series range
+    // uses the bare series, the other the guarded routine.
+    bool rev_exp = false;
+    if (lp_.present && cfg_.target == 0 && (!cfg_.f32 || cfg_.wide32))
+      for (int32_t j = 0; j < lp_.L; ++j)
+        rev_exp |= lp_.recompute[j] && lp_.tape_slot[j] < 0 && lp_.body[j].op == NT_EXP;
+    if (rev_exp) {
+      o_.open("if (!__any_sync(nt_lanes, nt_wide)) {");
+      series_exp_ = true;
+      for (int32_t o = 0; o < t_.n_out(); ++o) emit_reverse_for_output(o);
+      series_exp_ = false;
+      o_.close("} else {");
+      ++o_.ind;
+      for (int32_t o = 0; o < t_.n_out(); ++o) emit_reverse_for_output(o);
+      o_.close();
+    } else {
+      for (int32_t o = 0; o < t_.n_out(); ++o) emit_reverse_for_output(o);
+    }
+  }
 }
 
 std::string Emitter::run() {
   const bool host = cfg_.target == 1;
+  const bool mk = cfg_.markets;
   const int32_t nck_total = ckpt_values(p_);
   o_.line("// Generated by libnabla_b200 from a " + std::to_string(t_.n) + "-node tape.");
   if (host) {
@@ -529,25 +599,45 @@ std::string Emitter::run() {
   o_.line("#include \"nt_device_rt.cuh\"");
   o_.line(std::string("typedef ") + (cfg_.f32 ? "float" : "double") + " real;");
   o_.line("#define NT_CH " + std::to_string(channels()));
+  o_.line("#define NT_NIN " + std::to_string(std::max(1, t_.n_in())));
   const int32_t ntape = lp_.present ? lp_.n_tape : 0;
   o_.line("#define NT_NTAPE " + std::to_string(std::max(1, ntape)));
+  // Input registers: once per launch, or once per market in the multi-market
+  // variant (inputs[m * NT_NIN + j]).
+  auto load_inputs = [&](const std::string& base) {
+    for (int32_t j = 0; j < t_.n_in(); ++j)
+      o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + base + std::to_string(j) + "];");
+  };
   if (host) {
     o_.line("#define NT_CK(slot) nt_ckbuf[(slot)]");
     o_.line("#define NT_TAPE(u, slot) nt_tapebuf[(nt_u64)(u) * NT_NTAPE + (slot)]");
-    o_.open("extern \"C\" void nt_host_replay(const double* inputs, uint64_t n_paths, uint64_t path_offset, uint64_t seed, double* sums) {");
-    for (int32_t j = 0; j < t_.n_in(); ++j)
-      o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
-    o_.line("double nt_acc[NT_CH];");
-    o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = 0.0;");
+    if (mk)
+      o_.open("extern \"C\" void nt_host_replay_markets(const double* inputs, int n_states, uint64_t n_paths, "
+              "uint64_t path_offset, uint64_t seed, double* sums) {");
+    else
+      o_.open("extern \"C\" void nt_host_replay(const double* inputs, uint64_t n_paths, uint64_t path_offset, "
+              "uint64_t seed, double* sums) {");
+    if (!mk) load_inputs("");
+    const std::string nacc = mk ? "n_states * NT_CH" : "NT_CH";
+    o_.line("double* nt_acc = new double[" + nacc + "];");
+    o_.line("for (int c = 0; c < " + nacc + "; ++c) nt_acc[c] = 0.0;");
     o_.line("real nt_ckbuf[" + std::to_string(std::max(1, nck_total)) + "];");
     o_.line("(void)nt_ckbuf;");
     o_.line("real* nt_tapebuf = new real[" + std::to_string(std::max(1, (lp_.present ? lp_.N : 1) * std::max(1, ntape))) + "];");
     o_.line("(void)nt_tapebuf;");
     o_.open("for (nt_u64 p = 0; p < n_paths; ++p) {");
     o_.line("const nt_u64 path = p + path_offset;");
-    emit_scenario();
+    if (mk) {
+      o_.open("for (int nt_m = 0; nt_m < n_states; ++nt_m) {");
+      load_inputs("nt_m * NT_NIN + ");
+      emit_scenario();
+      o_.close();
+    } else {
+      emit_scenario();
+    }
     o_.close();
-    o_.line("for (int c = 0; c < NT_CH; ++c) sums[c] = nt_acc[c];");
+    o_.line("for (int c = 0; c < " + nacc + "; ++c) sums[c] = nt_acc[c];");
+    o_.line("delete[] nt_acc;");
     o_.line("delete[] nt_tapebuf;");
     o_.close();
     return o_.s;
@@ -569,10 +659,17 @@ std::string Emitter::run() {
   o_.line("#define NT_NLOOP " + std::to_string(lp_.present ? lp_.N : 0));
   o_.line("#define NT_TAPE(u, slot) nt_tape_b[((u) * NT_NTAPE + (slot)) * NT_BLOCK]");
   std::string bounds = "__launch_bounds__(NT_BLOCK" + (cfg_.min_blocks > 0 ? ", " + std::to_string(cfg_.min_blocks) : std::string()) + ")";
-  o_.line("extern \"C\" __global__ void " + bounds + " nt_replay_kernel(");
-  o_.line("    const double* __restrict__ inputs, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
-  o_.line("    double* __restrict__ partials, unsigned int* __restrict__ ticket, double* __restrict__ out,");
-  o_.line("    int accumulate, real* __restrict__ nt_gck, real* __restrict__ nt_tape) {");
+  if (mk) {
+    o_.line("extern \"C\" __global__ void " + bounds + " nt_markets_kernel(");
+    o_.line("    const double* __restrict__ inputs, int n_states, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
+    o_.line("    double* __restrict__ partials, unsigned int* __restrict__ ticket, double* __restrict__ out,");
+    o_.line("    int accumulate, real* __restrict__ nt_gck, real* __restrict__ nt_tape, double* __restrict__ nt_gacc) {");
+  } else {
+    o_.line("extern \"C\" __global__ void " + bounds + " nt_replay_kernel(");
+    o_.line("    const double* __restrict__ inputs, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
+    o_.line("    double* __restrict__ partials, unsigned int* __restrict__ ticket, double* __restrict__ out,");
+    o_.line("    int accumulate, real* __restrict__ nt_gck, real* __restrict__ nt_tape) {");
+  }
   ++o_.ind;
   if (!cfg_.global_ckpt) o_.line("extern __shared__ real nt_ck[];");
   o_.line("__shared__ double nt_red[NT_CH * (NT_BLOCK / 32)];");
@@ -588,37 +685,58 @@ std::string Emitter::run() {
             "NT_BLOCK);");
     o_.line("real* __restrict__ const nt_tape_b = nt_tape_blk + threadIdx.x;");
   }
-  for (int32_t j = 0; j < t_.n_in(); ++j)
-    o_.line("const real in" + std::to_string(j) + " = (real)inputs[" + std::to_string(j) + "];");
-  if (acc_smem_) {
-    // Compensated accumulators live in shared memory (one column per thread):
-    // they are touched once per scenario, so registers are better spent on
-    // the segment buffer and occupancy.
-    o_.line("__shared__ double nt_accs[2 * NT_CH * NT_BLOCK];");
-    o_.line("#define NT_ACC(k) nt_accs[(2 * (k)) * NT_BLOCK + threadIdx.x]");
-    o_.line("#define NT_CMP(k) nt_accs[(2 * (k) + 1) * NT_BLOCK + threadIdx.x]");
-    o_.line("for (int c = 0; c < NT_CH; ++c) { NT_ACC(c) = 0.0; NT_CMP(c) = 0.0; }");
+  if (mk) {
+    // Compensated per-market accumulators in a global block tile
+    // [block][2 * market * NT_CH + 2k (+1)][thread of block], zeroed by the
+    // host before the launch: touched once per scenario and market.
+    o_.line("double* __restrict__ const nt_gacc_b = nt_gacc + (nt_u64)blockIdx.x * ((nt_u64)2 * n_states * NT_CH * "
+            "NT_BLOCK) + threadIdx.x;");
+    o_.line("#define NT_ACC(k) nt_gacc_b[(nt_u64)(2 * (nt_m * NT_CH + (k))) * NT_BLOCK]");
+    o_.line("#define NT_CMP(k) nt_gacc_b[(nt_u64)(2 * (nt_m * NT_CH + (k)) + 1) * NT_BLOCK]");
   } else {
-    o_.line("double nt_acc[NT_CH], nt_cmp[NT_CH];");
-    o_.line("#pragma unroll");
-    o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
+    load_inputs("");
+    if (acc_smem_) {
+      // Compensated accumulators live in shared memory (one column per thread):
+      // they are touched once per scenario, so registers are better spent on
+      // the segment buffer and occupancy.
+      o_.line("__shared__ double nt_accs[2 * NT_CH * NT_BLOCK];");
+      o_.line("#define NT_ACC(k) nt_accs[(2 * (k)) * NT_BLOCK + threadIdx.x]");
+      o_.line("#define NT_CMP(k) nt_accs[(2 * (k) + 1) * NT_BLOCK + threadIdx.x]");
+      o_.line("for (int c = 0; c < NT_CH; ++c) { NT_ACC(c) = 0.0; NT_CMP(c) = 0.0; }");
+    } else {
+      o_.line("double nt_acc[NT_CH], nt_cmp[NT_CH];");
+      o_.line("#pragma unroll");
+      o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
+    }
   }
   o_.line("nt_math_tables_load();");
   o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
   o_.line("const nt_u64 path = p + path_offset;");
   o_.line("const unsigned nt_lanes = __activemask();");
   o_.line("(void)nt_lanes;");
-  emit_scenario();
-  o_.close();
-  if (acc_smem_) {
-    o_.line("double nt_acc[NT_CH];");
-    o_.line("#pragma unroll");
-    o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = NT_ACC(c) + NT_CMP(c);");
+  if (mk) {
+    o_.open("for (int nt_m = 0; nt_m < n_states; ++nt_m) {");
+    load_inputs("nt_m * NT_NIN + ");
+    emit_scenario();
+    o_.close();
   } else {
-    o_.line("#pragma unroll");
-    o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] += nt_cmp[c];");
+    emit_scenario();
   }
-  o_.line("nt_grid_reduce(nt_acc, NT_CH, nt_red, partials, ticket, out, accumulate);");
+  o_.close();
+  if (mk) {
+    o_.line("nt_grid_reduce_cols(nt_gacc_b, NT_BLOCK, n_states * NT_CH, NT_CH, nt_red, partials, ticket, out, "
+            "accumulate);");
+  } else {
+    if (acc_smem_) {
+      o_.line("double nt_acc[NT_CH];");
+      o_.line("#pragma unroll");
+      o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = NT_ACC(c) + NT_CMP(c);");
+    } else {
+      o_.line("#pragma unroll");
+      o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] += nt_cmp[c];");
+    }
+    o_.line("nt_grid_reduce(nt_acc, NT_CH, nt_red, partials, ticket, out, accumulate);");
+  }
   o_.close();
   return o_.s;
 }

@@ -188,6 +188,7 @@ void Exec::load(int max_regs) {
   if (prop.major != 10) fail(NT_E_UNSUPPORTED, std::string("this engine targets sm_100 (B200); device is ") + prop.name);
   sm_count = prop.multiProcessorCount;
   double secs = 0.0;
+  max_regs_opt = max_regs;
   std::vector<char> cubin = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs, cfg.fmad, max_regs);
   const auto t0 = std::chrono::steady_clock::now();
   Driver& d = driver();
@@ -271,9 +272,16 @@ Exec::~Exec() {
   cudaFree(d_red);
   cudaFree(d_gck);
   cudaFree(d_tape);
+  cudaFree(d_mk_inputs);
+  cudaFree(d_mk_acc);
+  cudaFree(d_mk_partials);
+  cudaFree(d_mk_out);
+  cudaFree(d_mk_gck);
+  cudaFree(d_mk_tape);
   if (h_stage) cudaFreeHost(h_stage);
   if (stream) cudaStreamDestroy(stream);
   if (module) driver().moduleUnload(module);
+  if (mk_module) driver().moduleUnload(mk_module);
 }
 
 // ---- launch ---------------------------------------------------------------------
@@ -328,6 +336,93 @@ void Exec::replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, 
   cuda_check(cudaMemcpyAsync(h_out, d_out, sizeof(double) * channels, cudaMemcpyDeviceToHost, stream), "read sums");
   cuda_check(cudaStreamSynchronize(stream), "replay");
   std::memcpy(sums, h_out, sizeof(double) * channels);
+  if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// ---- several markets in one launch (common random numbers) ----------------------
+//
+// The reference re-prices a shocked market by a full replay per market
+// (nablatensor-quant/.../scenario/ScenarioRunner.java:36-71), and its cpu-jit
+// engine can cache the draw block between such replays
+// (nablatensor-engine-cpu/.../jit/JitReplay.java:69-89).  Here one launch runs
+// every scenario under all markets in turn: the first market draws and tapes
+// the loop's normals, the others read them back, so Philox and Box-Muller are
+// paid once per scenario.  Sums per market equal separate replays with the same
+// seed (the same per-thread order, the same block-order reduction), up to the
+// rounding of multiply-adds the compiler fuses differently in the two kernels.
+
+void Exec::markets(int32_t n_states, const double* h_inputs, uint64_t paths, uint64_t offset, uint64_t seed,
+                   double* sums, double* seconds) {
+  if (n_states < 1 || n_states > 4096) fail(NT_E_INVALID_ARG, "n_states must be in [1, 4096]");
+  if (paths == 0) fail(NT_E_INVALID_ARG, "paths must be positive");
+  if (!h_inputs || !sums) fail(NT_E_INVALID_ARG, "inputs and sums must not be null");
+  const auto t0 = std::chrono::steady_clock::now();
+  bind();
+  Driver& d = driver();
+  if (!mk_function) {
+    // The multi-market kernel keeps the executable's plan, so its reverse
+    // sweep is the plain kernel's.  (Taping the draws only and recomputing
+    // each market's transcendentals in the reverse sweep moves half the bytes
+    // but needs more registers; it measured slower.)
+    EmitConfig mk = cfg;
+    mk.markets = true;
+    mk_plan = plan_tape(tape, mk);
+    const size_t real_bytes = cfg.f32 ? 4 : 8;
+    if (mk.global_ckpt && ckpt_values(mk_plan) > 0)
+      cuda_check(cudaMalloc(&d_mk_gck, (size_t)ckpt_values(mk_plan) * grid * cfg.block * real_bytes),
+                 "cudaMalloc market checkpoints");
+    if (mk_plan.loop.present && mk_plan.loop.n_tape > 0)
+      cuda_check(cudaMalloc(&d_mk_tape, (size_t)mk_plan.loop.N * mk_plan.loop.n_tape * grid * cfg.block * real_bytes),
+                 "cudaMalloc market value tape");
+    const int mk_smem = mk.global_ckpt ? 0 : (int)((size_t)ckpt_values(mk_plan) * cfg.block * real_bytes);
+    if (mk_smem != dyn_smem) fail(NT_E_INTERNAL, "multi-market plan changed the shared checkpoint size");
+    double secs = 0.0;
+    std::vector<char> cubin =
+        nvrtc_compile(emit(tape, mk_plan, mk), "sm_100a", use_disk_cache, &secs, cfg.fmad, max_regs_opt);
+    cu_check(d.moduleLoadData(&mk_module, cubin.data()), "cuModuleLoadData (markets)");
+    cu_check(d.moduleGetFunction(&mk_function, mk_module, "nt_markets_kernel"), "cuModuleGetFunction (markets)");
+    if (dyn_smem > 0)
+      cu_check(d.funcSetAttribute(mk_function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_smem),
+               "cuFuncSetAttribute (markets)");
+    cu_check(d.funcGetAttribute(&info.markets_registers, CU_FUNC_ATTRIBUTE_NUM_REGS, mk_function),
+             "cuFuncGetAttribute (markets)");
+    cu_check(d.funcGetAttribute(&info.markets_local_bytes, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, mk_function),
+             "cuFuncGetAttribute (markets)");
+  }
+  const size_t nin = (size_t)std::max<int32_t>(1, tape.n_in());
+  const size_t total = (size_t)n_states * (size_t)channels;
+  if ((size_t)n_states > mk_capacity) {
+    cudaFree(d_mk_inputs);
+    cudaFree(d_mk_acc);
+    cudaFree(d_mk_partials);
+    cudaFree(d_mk_out);
+    d_mk_inputs = d_mk_acc = d_mk_partials = d_mk_out = nullptr;
+    mk_capacity = 0;
+    cuda_check(cudaMalloc(&d_mk_inputs, sizeof(double) * nin * n_states), "cudaMalloc market inputs");
+    cuda_check(cudaMalloc(&d_mk_acc, sizeof(double) * 2 * total * (size_t)grid * cfg.block), "cudaMalloc market sums");
+    cuda_check(cudaMalloc(&d_mk_partials, sizeof(double) * total * (size_t)grid), "cudaMalloc market partials");
+    cuda_check(cudaMalloc(&d_mk_out, sizeof(double) * total), "cudaMalloc market out");
+    mk_capacity = (size_t)n_states;
+  }
+  if (tape.n_in() > 0)
+    cuda_check(cudaMemcpyAsync(d_mk_inputs, h_inputs, sizeof(double) * tape.n_in() * n_states,
+                               cudaMemcpyHostToDevice, stream),
+               "upload market inputs");
+  const unsigned g = grid_for(paths);
+  cuda_check(cudaMemsetAsync(d_mk_acc, 0, sizeof(double) * 2 * total * (size_t)g * cfg.block, stream),
+             "clear market sums");
+  void* gck = d_mk_gck;
+  void* tp = d_mk_tape;
+  int ns = n_states, accumulate = 0;
+  unsigned long long n = paths, off = offset, sd = seed;
+  void* args[] = {&d_mk_inputs, &ns, &n, &off, &sd, &d_mk_partials, &d_ticket, &d_mk_out, &accumulate, &gck, &tp,
+                  &d_mk_acc};
+  cu_check(d.launchKernel(mk_function, g, 1, 1, (unsigned)cfg.block, 1, 1, (unsigned)dyn_smem, (CUstream)stream, args,
+                          nullptr),
+           "cuLaunchKernel (markets)");
+  ++launches;
+  cuda_check(cudaMemcpyAsync(sums, d_mk_out, sizeof(double) * total, cudaMemcpyDeviceToHost, stream), "read sums");
+  cuda_check(cudaStreamSynchronize(stream), "markets replay");
   if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
 

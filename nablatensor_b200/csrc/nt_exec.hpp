@@ -25,6 +25,7 @@ struct Exec {
   std::string source;
   int device = -1;
   bool use_disk_cache = true;
+  int max_regs_opt = 0;  // nt_options.max_regs, kept for the kernels compiled later
   CUmodule module = nullptr;
   CUfunction function = nullptr;
   cudaStream_t stream = nullptr;
@@ -44,6 +45,18 @@ struct Exec {
   double compile_seconds = 0.0;
   uint64_t launches = 0;
   nt_exec_info info{};
+  // Multi-market kernel (compiled on first use) and its buffers, grown to
+  // the largest market count seen.
+  CUmodule mk_module = nullptr;
+  CUfunction mk_function = nullptr;
+  double* d_mk_inputs = nullptr;
+  double* d_mk_acc = nullptr;
+  double* d_mk_partials = nullptr;
+  double* d_mk_out = nullptr;
+  size_t mk_capacity = 0;  // markets the buffers hold
+  Plan mk_plan;            // draws-only value tape (see markets())
+  void* d_mk_gck = nullptr;
+  void* d_mk_tape = nullptr;
   // multi-GPU
   void* comm = nullptr;
   int32_t nranks = 1, rank = 0, dist_timeout_ms = 60000;
@@ -67,6 +80,9 @@ struct Exec {
   void sharded_enqueue(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk);
   void sharded(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk, double* sums, double* seconds);
   void attach(int32_t n, int32_t r, const uint8_t id[128], int32_t timeout_ms);
+  // One launch over `n_states` input vectors sharing each scenario's draws.
+  void markets(int32_t n_states, const double* inputs, uint64_t paths, uint64_t offset, uint64_t seed,
+               double* sums, double* seconds);
   void detach();
 };
 

@@ -104,12 +104,17 @@ struct EmitConfig {
   bool acc_smem = true;    // compensated accumulators in shared memory
   bool tape = true;        // expensive loop values go to a per-thread tape instead of being recomputed
   bool tape_all = true;    // tape draws and transcendentals (else draws only)
+  bool tape_every_exp = false;  // tape_all: also the exps of draws and invariants alone
   int32_t grid_blocks_per_sm = 0;  // 0: as many as fit
   int32_t fwd_unroll = 1;  // unroll of the forward unit loop
   int32_t block = 128;
   int32_t min_blocks = 0;
   int32_t seg_units = 0;   // 0 = automatic
   int32_t target = 0;      // 0 CUDA, 1 host C++
+  // Multi-market variant: one launch replays every scenario under n_states
+  // input vectors; the first state draws, later states read the draws back
+  // from the value tape (common random numbers).
+  bool markets = false;
 };
 
 // Emitter configuration from the C ABI options (validates them).

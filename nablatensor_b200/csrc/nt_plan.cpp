@@ -274,8 +274,11 @@ struct Weights {
 EmitConfig config_from(const nt_options* opt, int32_t target) {
   if (!opt) fail(NT_E_INVALID_ARG, "options are null");
   if (opt->precision != NT_FLOAT32 && opt->precision != NT_FLOAT64) fail(NT_E_INVALID_ARG, "bad precision");
-  if (target != 0 && target != 1) fail(NT_E_INVALID_ARG, "target must be 0 (CUDA) or 1 (host)");
+  if (target < 0 || target > 3)
+    fail(NT_E_INVALID_ARG, "target must be 0 (CUDA), 1 (host), 2 (CUDA multi-market) or 3 (host multi-market)");
   EmitConfig cfg;
+  cfg.markets = target >= 2;
+  target &= 1;
   cfg.f32 = opt->precision == NT_FLOAT32;
   cfg.adjoints = opt->adjoints != 0;
   cfg.no_loop = (opt->flags & NT_FLAG_NO_LOOP) != 0;
@@ -296,6 +299,8 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   cfg.acc_smem = (opt->flags & NT_FLAG_ACC_REGS) == 0;
   cfg.tape = (opt->flags & NT_FLAG_RECOMPUTE_ALL) == 0;
   cfg.tape_all = (opt->flags & NT_FLAG_TAPE_DRAWS) == 0;
+  cfg.tape_every_exp = (opt->flags & NT_FLAG_TAPE_ALL) != 0;
+  if (!cfg.tape_all && cfg.tape_every_exp) fail(NT_E_INVALID_ARG, "NT_FLAG_TAPE_DRAWS and NT_FLAG_TAPE_ALL conflict");
   if (opt->grid_blocks_per_sm < 0) fail(NT_E_INVALID_ARG, "grid_blocks_per_sm must be >= 0");
   cfg.grid_blocks_per_sm = opt->grid_blocks_per_sm;
   return cfg;
@@ -308,6 +313,7 @@ int32_t ckpt_values(const Plan& p) {
 Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
   Plan p;
   Loop& lp = p.loop;
+  int32_t per_unit = 0;  // values one unit's reverse sweep reads (register estimate)
   if (!cfg.no_loop) {
     Candidate c = find_loop(t);
     if (c.N >= 3) {
@@ -340,7 +346,6 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     // target; otherwise the remainder units are peeled into the epilogue.  The
     // automatic target keeps one segment's reverse-sweep values within about
     // 64 registers (the values a unit's reverse reads, 2 registers each in fp64).
-    int32_t per_unit = 0;
     if (units >= 2 && validate(t, B, L * U, nullptr) >= 2) {
       Loop probe;
       probe.present = true;
@@ -403,12 +408,32 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
       }
     }
     // Recompute closure: nodes needed to regenerate the stored values.  In
-    // tape mode an expensive node (a draw, exp, log, sqrt or division) is a
-    // leaf: the forward sweep writes its value to the thread's tape and the
-    // reverse sweep reads it back instead of recomputing its inputs.
-    auto expensive = [&](int op) {
+    // tape mode an expensive node is a leaf: the forward sweep writes its value
+    // to the thread's tape and the reverse sweep reads it back instead of
+    // recomputing its inputs.  Expensive are the draws, and (unless only draws
+    // are taped) log, sqrt, division, and an exp whose argument depends on a
+    // loop carry.  An exp of the unit's draws and loop invariants alone -- a
+    // GBM log-return -- is recomputed: its argument is small, the reverse sweep
+    // evaluates it by the branch-free series, and that is cheaper than moving
+    // 16 bytes per value through HBM.  Not in a unit whose reverse values
+    // already fill the register budget on their own (more than 32 registers,
+    // one unit per segment, e.g. a 10-asset basket step): there the recompute
+    // lengthens a latency-bound sweep, and the tape wins.
+    const bool light_unit = per_unit * (cfg.f32 ? 1 : 2) <= 32;
+    std::vector<uint8_t> carry_dep(L, 0);
+    for (int32_t j = 0; j < L; ++j) {
+      const BodyNode& bn = lp.body[j];
+      for (int w = 0; w < nargs(bn.op); ++w) {
+        const Ref& r = w == 0 ? bn.ra : bn.rb;
+        if (r.kind == REF_CARRY || (r.kind == REF_SAME && carry_dep[r.idx])) carry_dep[j] = 1;
+      }
+    }
+    auto expensive = [&](int32_t j) {
+      const int op = lp.body[j].op;
       if (op == NT_RANDN || op == NT_RANDU) return true;
-      return cfg.tape_all && (op == NT_EXP || op == NT_LOG || op == NT_SQRT || op == NT_DIV);
+      if (!cfg.tape_all) return false;
+      if (op == NT_LOG || op == NT_SQRT || op == NT_DIV) return true;
+      return op == NT_EXP && (carry_dep[j] != 0 || cfg.tape_every_exp || !light_unit);
     };
     std::vector<uint8_t> need(lp.stored);
     lp.tape_slot.assign(L, -1);
@@ -417,7 +442,7 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
       for (int32_t j = L - 1; j >= 0; --j) {
         if (!need[j]) continue;
         const BodyNode& bn = lp.body[j];
-        if (cfg.tape && expensive(bn.op)) continue;  // a tape leaf
+        if (cfg.tape && expensive(j)) continue;  // a tape leaf
         for (int w = 0; w < nargs(bn.op); ++w) {
           const Ref& r = w == 0 ? bn.ra : bn.rb;
           if ((r.kind == REF_SAME || r.kind == REF_CARRY) && !need[r.idx]) { need[r.idx] = 1; changed = true; }
@@ -429,7 +454,7 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     lp.n_tape = 0;
     if (cfg.tape)
       for (int32_t j = 0; j < L; ++j)
-        if (need[j] && expensive(lp.body[j].op)) lp.tape_slot[j] = lp.n_tape++;
+        if (need[j] && expensive(j)) lp.tape_slot[j] = lp.n_tape++;
     lp.ckpt.clear();
     for (int32_t k : lp.carries)
       if (carry_read[k]) lp.ckpt.push_back(k);

@@ -168,7 +168,7 @@ _ENGINE_KEYS = {"block": "block", "segUnits": "seg_units", "minBlocks": "min_blo
 _ENGINE_FLAGS = {"noLoop": _lib.NT_FLAG_NO_LOOP, "sharedCheckpoints": _lib.NT_FLAG_SHARED_CKPT,
                  "fp32Fast": _lib.NT_FLAG_F32_FAST, "noFmad": _lib.NT_FLAG_NO_FMAD,
                  "accRegisters": _lib.NT_FLAG_ACC_REGS, "recomputeAll": _lib.NT_FLAG_RECOMPUTE_ALL,
-                 "tapeDraws": _lib.NT_FLAG_TAPE_DRAWS}
+                 "tapeDraws": _lib.NT_FLAG_TAPE_DRAWS, "tapeAll": _lib.NT_FLAG_TAPE_ALL}
 
 
 class B200AadExecutable(AadExecutable):
@@ -213,7 +213,9 @@ class B200AadExecutable(AadExecutable):
         return self._info["compile_seconds"]
 
     def info(self) -> dict:
-        return dict(self._info)
+        info = _lib.NtExecInfo()
+        _lib.check(_lib.lib().nt_exec_info_get(self._handle(), ctypes.byref(info)))
+        return info.as_dict()
 
     def source(self) -> str:
         n = ctypes.c_size_t(0)
@@ -258,6 +260,60 @@ class B200AadExecutable(AadExecutable):
         """One dispatch over [path_offset, path_offset + paths) (AadExecutable.java:46-47)."""
         sums, secs = self.replay_sums(paths, path_offset, seed)
         return AadResult.from_sums(sums, self._tape, paths, secs)
+
+    def _market_matrix(self, markets) -> np.ndarray:
+        """Input vectors for nt_replay_markets: each market is a full input
+        vector, or a dict of named inputs overriding the current inputs."""
+        names = self._tape.input_names
+        rows = []
+        for m in markets:
+            if isinstance(m, dict):
+                row = np.asarray(self._inputs, dtype=np.float64).copy()
+                for k, v in m.items():
+                    if k not in names:
+                        raise ValueError(f"unknown input: {k}")
+                    row[names.index(k)] = float(v)
+            else:
+                row = np.asarray(m, dtype=np.float64)
+                if row.shape != (len(names),):
+                    raise ValueError(f"expected {len(names)} inputs per market")
+            rows.append(row)
+        if not rows:
+            raise ValueError("at least one market is needed")
+        return np.ascontiguousarray(np.stack(rows), dtype=np.float64)
+
+    def replayMarkets_sums(self, markets, paths: int, path_offset: int, seed: int):
+        if paths <= 0:
+            raise ValueError("paths must be positive")
+        x = self._market_matrix(markets)
+        sums = np.zeros((x.shape[0], self._channels), dtype=np.float64)
+        secs = ctypes.c_double(0.0)
+        _lib.check(_lib.lib().nt_replay_markets(self._handle(), x.shape[0], _lib.ptr(x, ctypes.c_double), paths,
+                                                path_offset & (2**64 - 1), seed & (2**64 - 1),
+                                                _lib.ptr(sums, ctypes.c_double), ctypes.byref(secs)))
+        return sums, secs.value
+
+    def replayMarkets(self, markets, paths: int, path_offset: int, seed: int) -> List[AadResult]:
+        """Re-prices under every market in one dispatch with common random
+        numbers (nt_replay_markets): the per-market loop of
+        ScenarioRunner.run (nablatensor-quant/.../scenario/ScenarioRunner.java:36-53)
+        without a replay per market.  Each result equals replay() under that
+        market's inputs with the same seed, up to the rounding of fused
+        multiply-adds (1e-13 relative in fp64)."""
+        sums, secs = self.replayMarkets_sums(markets, paths, path_offset, seed)
+        return [AadResult.from_sums(s, self._tape, paths, secs) for s in sums]
+
+    def ladder(self, name: str, values: Sequence[float], paths: int, path_offset: int, seed: int):
+        """A 1-D ladder over one input, the others at their current values
+        (ScenarioRunner.ladder, ScenarioRunner.java:58-71): returns
+        (x, price, greek of `name`) arrays, all from one dispatch."""
+        if name not in self._tape.input_names:
+            raise ValueError(f"unknown input: {name}")
+        x = [float(v) for v in values]
+        res = self.replayMarkets([{name: v} for v in x], paths, path_offset, seed)
+        price = np.array([r.value() for r in res])
+        greek = np.array([r.gradient(name) for r in res])
+        return np.array(x), price, greek
 
     def calibrate(self, seed: int) -> float:
         """AbstractAadExecutable.calibrate: probe dispatches growing x8."""

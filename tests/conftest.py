@@ -38,9 +38,11 @@ def oracle_mod():
 _HOST_DIR = os.path.join(tempfile.gettempdir(), "nt_host_kernels")
 
 
-def host_kernel(source: str):
+def host_kernel(source: str, markets: bool = False):
     """Compiles an nt_emit_source(target=1) program with g++ (no FMA
-    contraction, like the Java reference) and returns its nt_host_replay."""
+    contraction, like the Java reference) and returns its nt_host_replay
+    (markets=True: a target=3 program and its nt_host_replay_markets, taking
+    an [n_markets][n_in] input matrix and returning [n_markets][channels])."""
     os.makedirs(_HOST_DIR, exist_ok=True)
     key = hashlib.sha1(source.encode()).hexdigest()[:16]
     src = os.path.join(_HOST_DIR, key + ".cpp")
@@ -53,6 +55,20 @@ def host_kernel(source: str):
                        check=True)
         os.replace(so + ".tmp", so)
     lib = ctypes.CDLL(so)
+    if markets:
+        fm = lib.nt_host_replay_markets
+        fm.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64,
+                       ctypes.c_uint64, ctypes.POINTER(ctypes.c_double)]
+        fm.restype = None
+
+        def run_markets(inputs, paths, offset, seed, channels):
+            x = np.ascontiguousarray(inputs, dtype=np.float64)
+            sums = np.zeros((x.shape[0], channels), dtype=np.float64)
+            fm(x.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), x.shape[0], paths, offset & (2**64 - 1),
+               seed & (2**64 - 1), sums.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+            return sums
+        run_markets.lib = lib
+        return run_markets
     fn = lib.nt_host_replay
     fn.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
                    ctypes.POINTER(ctypes.c_double)]

@@ -93,7 +93,7 @@ def test_invalid_arguments(ntlib):
     f, c = ctypes.c_uint64(), ctypes.c_uint64()
     assert L.nt_shard_range(10, 0, 0, 0, ctypes.byref(f), ctypes.byref(c)) == _lib.NT_E_INVALID_ARG
     with pytest.raises(_lib.NablaError) as e:
-        _lib.emit_source(quant.asian_tape(4), target=2)
+        _lib.emit_source(quant.asian_tape(4), target=4)
     assert e.value.code == _lib.NT_E_INVALID_ARG
     for regs in (8, 256, -1):
         with pytest.raises(_lib.NablaError) as e:
@@ -113,6 +113,14 @@ def test_bad_block_size_is_an_argument_error(ntlib):
 def test_emitted_kernels_compile_for_sm100a(ntlib, make, f32):
     src = _lib.emit_source(make(), target=0, precision=0 if f32 else 1)
     assert "nt_replay_kernel" in src and "__launch_bounds__" in src
+    assert _lib.nvrtc_check(src) > 1000
+
+
+@pytest.mark.parametrize("make,f32", [(lambda: quant.asian_tape(252), False), (lambda: quant.barrier_tape(252), True),
+                                      (lambda: quant.basket_tape(), False), (every_op_tape, False)])
+def test_multi_market_kernels_compile_for_sm100a(ntlib, make, f32):
+    src = _lib.emit_source(make(), target=2, precision=0 if f32 else 1)
+    assert "nt_markets_kernel" in src and "nt_grid_reduce_cols" in src
     assert _lib.nvrtc_check(src) > 1000
 
 

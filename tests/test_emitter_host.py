@@ -48,6 +48,20 @@ def test_asian_loop_is_bit_exact(oracle_mod, seg_units):
     assert "step loop: 126 units" in src
 
 
+@pytest.mark.parametrize("flags,slots", [(0, 2), (_lib.NT_FLAG_TAPE_ALL, 4), (_lib.NT_FLAG_TAPE_DRAWS, 2),
+                                         (_lib.NT_FLAG_RECOMPUTE_ALL, 0)])
+def test_tape_plans_are_bit_exact(oracle_mod, flags, slots):
+    """Every reverse-sweep storage plan reproduces the oracle: by default the
+    normals are taped and the GBM exps (draws and invariants only) are
+    recomputed; the barrier's smoothing exps, which read the spot carry, stay
+    taped."""
+    src = _run(oracle_mod, quant.asian_tape(252), ATM, 1_500, 3, 42, flags=flags)
+    assert f"#define NT_NTAPE {max(1, slots)}" in src
+    bsrc = _run(oracle_mod, quant.barrier_tape(60), ATM, 1_000, 3, 42, flags=flags)
+    if flags == 0:
+        assert "#define NT_NTAPE 6" in bsrc  # 2 normals + 2 x 2 smoothing exps per unit
+
+
 def test_asian_straight_line_is_bit_exact(oracle_mod):
     src = _run(oracle_mod, quant.asian_tape(64), ATM, 2_000, 7, 42, flags=_lib.NT_FLAG_NO_LOOP)
     assert "step loop" not in src

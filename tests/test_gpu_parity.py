@@ -168,25 +168,29 @@ def test_loop_and_straight_line_kernels_agree(engine):
 
 
 def test_shared_checkpoints_and_recompute_all_agree(engine):
-    """The three reverse-sweep storage plans give the same sums: value tape +
-    L2 checkpoints (default), shared-memory checkpoints, and recomputing every
-    loop value from the checkpoints (no tape)."""
+    """The reverse-sweep storage plans give the same sums: value tape + L2
+    checkpoints (default: normals taped, GBM exps recomputed), shared-memory
+    checkpoints, recomputing every loop value from the checkpoints (no tape),
+    draws only, and every transcendental taped."""
     tape = quant.asian_tape(252)
     with engine.compile(tape, FP64) as a, \
             engine.compile(tape, FP64.with_engine_option("cuda", "sharedCheckpoints", "true")) as b, \
             engine.compile(tape, FP64.with_engine_option("cuda", "recomputeAll", "true")) as c, \
-            engine.compile(tape, FP64.with_engine_option("cuda", "tapeDraws", "true")) as d:
-        assert a.info()["ckpt_global"] == 1 and a.info()["tape_slots"] == 4  # normals and exps per unit
+            engine.compile(tape, FP64.with_engine_option("cuda", "tapeDraws", "true")) as d, \
+            engine.compile(tape, FP64.with_engine_option("cuda", "tapeAll", "true")) as e:
+        assert a.info()["ckpt_global"] == 1 and a.info()["tape_slots"] == 2  # the two normals per unit
         assert b.info()["ckpt_global"] == 0
         assert c.info()["tape_slots"] == 0
-        assert d.info()["tape_slots"] == 2  # the two normals only
+        assert d.info()["tape_slots"] == 2
+        assert e.info()["tape_slots"] == 4  # normals and exps
         x, _ = a.replay_sums(30_000, 5, 6)
         y, _ = b.replay_sums(30_000, 5, 6)
         z, _ = c.replay_sums(30_000, 5, 6)
         w, _ = d.replay_sums(30_000, 5, 6)
+        v, _ = e.replay_sums(30_000, 5, 6)
     np.testing.assert_allclose(x, y, rtol=1e-15)
-    np.testing.assert_allclose(x, z, rtol=2e-12)
-    np.testing.assert_allclose(x, w, rtol=2e-12)
+    for other in (z, w, v):
+        np.testing.assert_allclose(x, other, rtol=2e-12)
 
 
 @pytest.mark.parametrize("make,inputs,seed", [
@@ -216,6 +220,50 @@ def test_basket_config4_fp64(engine, oracle_mod):
         got, _ = ex.replay_sums(20_000, 0x1_0000_0003, 7)
     want, scale = _oracle(oracle_mod, tape, tape.recordedInputs(), 20_000, 0x1_0000_0003, 7)
     _assert_parity(got, want, scale)
+
+
+@pytest.mark.parametrize("make,base,f32", [
+    (lambda: quant.asian_tape(252), ATM, False),
+    (lambda: quant.barrier_tape(252), ATM, True),
+    (lambda: quant.basket_tape(), None, False),
+])
+def test_markets_equal_separate_replays(engine, oracle_mod, make, base, f32):
+    """nt_replay_markets: each market's sums equal a plain replay under that
+    market's inputs (same draws, per-thread order and block-order reduction).
+    The multi-market kernel recomputes the transcendentals the plain kernel
+    tapes, and the compiler may fuse a multiply-add differently there, so the
+    bound is the rounding of that: 1e-13 in fp64, 1e-6 in fp32 (the host build,
+    without contraction, is bit-exact: test_markets_host.py).  The first market
+    also matches the oracle."""
+    tape = make()
+    base = list(tape.recordedInputs()) if base is None else base
+    markets = [list(base)]
+    for j, f in [(0, 0.9), (0, 1.1), (2, 1.3), (1, 1.02)]:
+        x = list(base)
+        x[j] *= f
+        markets.append(x)
+    paths, off, seed = 60_000, 0x1_0000_0003, 42
+    with engine.compile(tape, FP32 if f32 else FP64) as ex:
+        got, _ = ex.replayMarkets_sums(markets, paths, off, seed)
+        for m, x in enumerate(markets):
+            ex.setInputs(x)
+            want, _ = ex.replay_sums(paths, off, seed)
+            np.testing.assert_allclose(got[m], want, rtol=1e-6 if f32 else 1e-13, atol=0, err_msg=f"market {m}")
+    if not f32:
+        want, scale = _oracle(oracle_mod, tape, markets[0], paths, off, seed)
+        _assert_parity(got[0], want, scale)
+
+
+def test_ladder_over_spot(engine):
+    tape = quant.asian_tape(252)
+    with engine.compile(tape, FP64) as ex:
+        ex.setInputs(ATM)
+        x, price, delta = ex.ladder("spot", [90.0, 100.0, 110.0], 200_000, 0, 42)
+        ex.setInputs([110.0] + ATM[1:])
+        r = ex.replay(200_000, 0, 42)
+    assert np.all(np.diff(price) > 0) and np.all(delta > 0)
+    assert price[2] == pytest.approx(r.value(), rel=1e-13)
+    assert delta[2] == pytest.approx(r.gradient("spot"), rel=1e-13)
 
 
 def test_replay_safe_matches_single_dispatch(engine):
