@@ -163,6 +163,7 @@ Exec* Exec::create(const nt_tape* tape, const nt_options* opt) {
   x->device = opt->device;
   x->use_disk_cache = (opt->flags & NT_FLAG_NO_DISK_CACHE) == 0;
   x->plan = plan_tape(x->tape, x->cfg);
+  if (opt->block == 0) x->cfg.block = auto_block(x->plan);
   x->channels = x->tape.n_out() * (2 + x->tape.n_in());
   const size_t real_bytes = x->cfg.f32 ? 4 : 8;
   // Checkpoints in shared memory unless they would starve occupancy.

@@ -92,6 +92,7 @@ struct Plan {
   double fwd_flops = 0.0;  // algorithmic, per scenario
   double rev_flops = 0.0;
   int32_t stored_per_unit = 0;
+  int32_t per_unit_regs = 0;  // registers one loop unit's reverse values take (estimate)
 };
 
 struct EmitConfig {
@@ -125,6 +126,12 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg);
 
 // Emits CUDA C (target 0) or host C++ (target 1) for the plan.
 std::string emit(const Tape& t, const Plan& p, const EmitConfig& cfg);
+// Threads per block when nt_options.block is 0: 256 for a loop whose units are
+// light (their reverse values take <= 32 registers: larger blocks give the
+// bulk prefetches longer tiles at the same occupancy), 64 for heavier units
+// (a register-bound kernel keeps more, smaller blocks resident), 128 without a
+// loop.
+int32_t auto_block(const Plan& p);
 
 // Number of checkpointed values per thread for this plan (shared/global sizing).
 int32_t ckpt_values(const Plan& p);

@@ -306,6 +306,11 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   return cfg;
 }
 
+int32_t auto_block(const Plan& p) {
+  if (!p.loop.present) return 128;
+  return p.per_unit_regs <= 32 ? 256 : 64;
+}
+
 int32_t ckpt_values(const Plan& p) {
   return p.loop.present ? p.loop.K * (int32_t)p.loop.ckpt.size() : 0;
 }
@@ -419,7 +424,8 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     // already fill the register budget on their own (more than 32 registers,
     // one unit per segment, e.g. a 10-asset basket step): there the recompute
     // lengthens a latency-bound sweep, and the tape wins.
-    const bool light_unit = per_unit * (cfg.f32 ? 1 : 2) <= 32;
+    p.per_unit_regs = per_unit * (cfg.f32 ? 1 : 2);
+    const bool light_unit = p.per_unit_regs <= 32;
     std::vector<uint8_t> carry_dep(L, 0);
     for (int32_t j = 0; j < L; ++j) {
       const BodyNode& bn = lp.body[j];
