@@ -5,12 +5,12 @@ scenario ranges sharded across the GPUs with one NCCL all-reduce of the
 7 fp64 accumulators.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload asian1e9|asian2m|barrier20m|basket10m]
+                    [--workload asian1e9|asian2m|barrier20m|basket10m|cva1m]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 The default workload is config 3 above; `--workload` times the other
 BASELINE configurations (1: Asian 2M, 2: fp32 barrier 20M, 4: 10-asset
-basket 10M) with the same JSON line.
+basket 10M, 5: CVA of a 100-swap book 1M) with the same JSON line.
 
 Prints one JSON line on rank 0.  `value` is whole-job scenarios/s timed with
 CUDA events on the engine's stream (inputs resident, max over ranks); `e2e`
@@ -81,6 +81,11 @@ WORKLOADS = {w.name: w for w in [
              "sigma=0.2 r=0.03 T=1, value + 5 Greeks, 20,000,000 scenarios per step, seed 42 (fp32 nodes; "
              "exp/log/Box-Muller evaluated in fp64 and narrowed, the reference's fp32 semantics)",
              "barrier_fp32_replay_ncu.md"),
+    Workload("cva1m", 5, lambda q: q.cva_tape(), None, False, 1e6, 0, 11, 0.02,
+             "BASELINE config 5: fp64 CVA of 100 payer swaps (notionals U[1e6,1e8], fixed N(3%,0.5%), maturities "
+             "U[1,10]y on a semi-annual grid), one-factor Hull-White a=0.05 sigma=0.01, 40-pillar zero curve flat "
+             "3% + N(0,25bp) seed 11, 120 monthly dates, hazard 2%, recovery 40%, 1,000,000 scenarios per step, "
+             "adjoints w.r.t. the 40 pillars and the hazard rate", "cva_fp64_replay_ncu.md"),
     Workload("basket10m", 4, lambda q: q.basket_tape(), None, False, 1e7, 0, 7, 0.12,
              "BASELINE config 4: fp64 10-asset basket call, Cholesky of equicorrelation rho=0.5, spots U[80,120] "
              "and vols U[0.15,0.40] from seed 7, equal weights, K=100 r=0.03 T=1, 52 weekly steps, value + 21 "

@@ -335,7 +335,10 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     // forward sweep; the recompute itself takes the series when none was.
     if (recompute) exp_fn_ = series_exp_ ? "NT_EXP64_SERIES(" : "NT_EXP64(";
     else if (lp_.recompute[j] && lp_.tape_slot[j] < 0) exp_fn_ = "NT_EXP64W(";
-    o_.line(name(j) + " = " + fwd_expr(bn.op, A, B, bn.c, -1) + ";");
+    if (bn.op == NT_CONST && bn.cslot >= 0)
+      o_.line(name(j) + " = NT_CTAB(" + unit + ", " + std::to_string(bn.cslot) + ");");
+    else
+      o_.line(name(j) + " = " + fwd_expr(bn.op, A, B, bn.c, -1) + ";");
     exp_fn_ = "NT_EXP64(";
     emitted[j] = 1;
   }
@@ -602,6 +605,25 @@ std::string Emitter::run() {
   o_.line("#define NT_NIN " + std::to_string(std::max(1, t_.n_in())));
   const int32_t ntape = lp_.present ? lp_.n_tape : 0;
   o_.line("#define NT_NTAPE " + std::to_string(std::max(1, ntape)));
+  if (lp_.present && lp_.n_vary > 0) {
+    // Loop constants that change from unit to unit (a non-uniform time grid,
+    // per-date weights): one row per unit.  Every thread reads the same row at
+    // the same time, so the loads are broadcasts from L1.
+    o_.line("#define NT_NVARY " + std::to_string(lp_.n_vary));
+    o_.line(std::string(host ? "static const real" : "__device__ const real") + " nt_ctab[" +
+            std::to_string(lp_.ctab.size()) + "] = {");
+    std::string row;
+    for (size_t k = 0; k < lp_.ctab.size(); ++k) {
+      row += "(real)" + lit(lp_.ctab[k], false) + ",";
+      if (row.size() > 100 || k + 1 == lp_.ctab.size()) {
+        o_.line("  " + row);
+        row.clear();
+      }
+    }
+    o_.line("};");
+    o_.line(std::string("#define NT_CTAB(u, k) ") + (host ? "nt_ctab" : "__ldg(&nt_ctab") +
+            "[(u) * NT_NVARY + (k)]" + (host ? "" : ")"));
+  }
   // Input registers: once per launch, or once per market in the multi-market
   // variant (inputs[m * NT_NIN + j]).
   auto load_inputs = [&](const std::string& base) {

@@ -59,6 +59,7 @@ struct BodyNode {
   int32_t stream = 0;       // draws
   int32_t draw_base = 0;    // ordinal in unit 0
   int32_t draw_stride = 0;  // ordinal increase per unit
+  int32_t cslot = -1;       // CONST whose value differs between units: column of Loop::ctab
   bool active = false;      // OR over all units
 };
 
@@ -79,6 +80,8 @@ struct Loop {
   std::vector<uint8_t> recompute;   // per offset: recomputed from the segment checkpoint
   std::vector<int32_t> tape_slot;   // per offset: slot in the per-thread value tape, or -1
   int32_t n_tape = 0;               // taped values per unit
+  int32_t n_vary = 0;               // CONST offsets whose value differs between units
+  std::vector<double> ctab;         // their values, [unit][cslot] (a non-uniform time grid, date tables)
   int32_t G = 0;                    // units per segment
   int32_t K = 0;                    // segments (N = K * G)
   int32_t end() const { return B + N * L; }

@@ -39,7 +39,7 @@ bool compat(const Tape& t, int32_t i, int32_t L) {
   const int op = t.op[i];
   if (t.op[j] != op) return false;
   if (op == NT_INPUT) return false;
-  if (op == NT_CONST) return same_double(t.c[i], t.c[j]);
+  if (op == NT_CONST) return true;  // a constant may change from unit to unit (per-unit table)
   if (is_draw(op)) return t.b[i] == t.b[j] && t.a[j] > t.a[i];
   for (int w = 0; w < nargs(op); ++w) {
     const int32_t x = arg(t, i, w), y = arg(t, j, w);
@@ -63,7 +63,6 @@ int32_t validate(const Tape& t, int32_t B, int32_t L, int32_t* ncarries) {
     const int32_t i1 = B + L + j, i0 = B + j;
     const int op = t.op[i1];
     if (t.op[i0] != op || op == NT_INPUT) return 0;
-    if (op == NT_CONST && !same_double(t.c[i0], t.c[i1])) return 0;
     if (is_draw(op)) {
       if (t.b[i0] != t.b[i1]) return 0;
       stride[j] = t.a[i1] - t.a[i0];
@@ -97,7 +96,7 @@ int32_t validate(const Tape& t, int32_t B, int32_t L, int32_t* ncarries) {
       const int32_t i = (int32_t)base + j, i0 = B + j;
       const int op = t.op[i];
       if (op != t.op[i0]) { ok = false; break; }
-      if (op == NT_CONST) { ok = same_double(t.c[i], t.c[i0]); continue; }
+      if (op == NT_CONST) continue;
       if (is_draw(op)) {
         ok = t.b[i] == t.b[i0] && (int64_t)t.a[i] == (int64_t)t.a[i0] + (int64_t)N * stride[j];
         continue;
@@ -223,6 +222,20 @@ void describe(const Tape& t, Loop& lp) {
       lp.carries.push_back(k);
       lp.carry_init.push_back(init[k]);
     }
+  // Constants that differ between units go to the per-unit table.
+  lp.n_vary = 0;
+  for (int32_t j = 0; j < L; ++j) {
+    BodyNode& bn = lp.body[j];
+    if (bn.op != NT_CONST) continue;
+    bool same = true;
+    for (int32_t u = 1; u < N && same; ++u) same = same_double(t.c[B + u * L + j], t.c[B + j]);
+    bn.c = t.c[B + j];
+    if (!same) bn.cslot = lp.n_vary++;
+  }
+  lp.ctab.assign((size_t)N * lp.n_vary, 0.0);
+  for (int32_t j = 0; j < L; ++j)
+    if (lp.body[j].cslot >= 0)
+      for (int32_t u = 0; u < N; ++u) lp.ctab[(size_t)u * lp.n_vary + lp.body[j].cslot] = t.c[B + u * L + j];
   const int32_t end = B + N * L;
   auto mark = [&](int32_t x) {
     if (x >= B && x < end) lp.is_exit[(x - B) % L] = 1;

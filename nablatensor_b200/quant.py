@@ -317,6 +317,142 @@ def barrier_tape(steps: int = 252, level: float = 80.0, width: float = 1.0, kind
                         TimeGrid.uniform_grid(steps))
 
 
+# ---- CVA of an interest-rate swap book under one-factor Hull-White --------------
+#
+# The reference records CVA path by path and trade by trade
+# (nablatensor-cva/.../ExposureSimulation.java:121-229, InterestRateSwap.java:129-154,
+# HwShortRate.java): every exposure date values each swap's remaining coupons, so
+# no two dates record the same nodes.  The book here is the BASELINE config-5
+# book -- 100 spot-starting payer swaps on a semi-annual grid, a 40-pillar zero
+# curve -- and its netted value is the same sum regrouped by payment date, so
+# every monthly date records one identical body and only its constants change
+# (which coupons are still alive, the bond coefficients of that date).  The
+# loop planner then keeps those constants in a per-date table.
+#
+#   x_k   = x_{k-1} e^{-a dt} + sigma sqrt((1 - e^{-2a dt}) / 2a) z_k   (exact OU step)
+#   I_k   = I_{k-1} + (x_{k-1} + x_k) dt / 2                           (integral of x)
+#   lp_k  = ln P(0, t_k) = sum_i C_ki zeta_i                          (zero rates zeta_i at the pillars)
+#   P_kj  = P(t_k, T_j) = exp(lp(T_j) - lp_k + A(t_k, T_j) - B(t_k, T_j) x_k)
+#   V_k   = A0_k - sum_j W_kj P_kj                                     (netted payer value, in millions)
+#   D_k   = exp(lp_k - I_k - V(0, t_k) / 2)                              (stochastic discount)
+#   CVA  += LGD max(V_k, 0) D_k S_{k-1} (1 - e^{-lambda dt}),   S_k = S_{k-1} e^{-lambda dt}
+#
+# with B, A and V(t, T) the Hull-White x-representation coefficients
+# (Brigo and Mercurio, Interest Rate Models, 2nd ed., section 3.3).
+
+MONEY_UNIT = 1.0e6  # the tape carries values in millions (ExposureSimulation.java:61-69)
+
+
+@dataclass
+class SwapBook:
+    notional: np.ndarray   # per swap
+    fixed_rate: np.ndarray
+    maturity: np.ndarray   # years, on the semi-annual payment grid
+
+    @staticmethod
+    def config5(n: int = 100, seed: int = 11, accrual: float = 0.5) -> "SwapBook":
+        g = np.random.Generator(np.random.PCG64(seed + 1))
+        notional = g.uniform(1e6, 1e8, n)
+        fixed = g.normal(0.03, 0.005, n)
+        mat = np.clip(np.round(g.uniform(1.0, 10.0, n) / accrual) * accrual, accrual, 10.0)
+        return SwapBook(notional, fixed, mat)
+
+
+def cva_config5_curve(pillars: int = 40, seed: int = 11):
+    """Zero rates at T_i = 0.25 i: flat 3% + N(0, 25bp), PCG64 seed 11."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    return [0.25 * (i + 1) for i in range(pillars)], [float(z) for z in 0.03 + g.normal(0.0, 0.0025, pillars)]
+
+
+def _curve_weights(t: float, tenors: Sequence[float]) -> np.ndarray:
+    """ln P(0, t) = -t zeta(t) as weights on the pillar zero rates: zeta
+    linear between pillars, flat outside."""
+    w = np.zeros(len(tenors))
+    if t <= tenors[0]:
+        w[0] = -t
+    elif t >= tenors[-1]:
+        w[-1] = -t
+    else:
+        i = int(np.searchsorted(tenors, t)) - 1
+        f = (t - tenors[i]) / (tenors[i + 1] - tenors[i])
+        w[i], w[i + 1] = -t * (1.0 - f), -t * f
+    return w
+
+
+def cva_tape(dates: int = 120, horizon: float = 10.0, a: float = 0.05, sigma: float = 0.01, hazard: float = 0.02,
+             recovery: float = 0.4, book: SwapBook = None, pillars: int = 40, seed: int = 11,
+             accrual: float = 0.5) -> AadTape:
+    """CVA of the swap book, adjoints w.r.t. the pillar zero
+    rates and the hazard rate (41 inputs)."""
+    book = book if book is not None else SwapBook.config5(seed=seed, accrual=accrual)
+    tenors, zeros = cva_config5_curve(pillars, seed)
+    dt = horizon / dates
+    pay = [accrual * (j + 1) for j in range(int(round(horizon / accrual)))]
+
+    def Bf(t, T):
+        return (1.0 - math.exp(-a * (T - t))) / a
+
+    def Vf(t, T):
+        tau = T - t
+        return sigma ** 2 / a ** 2 * (tau + 2.0 / a * math.exp(-a * tau) - 0.5 / a * math.exp(-2.0 * a * tau)
+                                      - 1.5 / a)
+
+    def Af(t, T):
+        return 0.5 * (Vf(t, T) - Vf(0.0, T) + Vf(0.0, t))
+
+    ea = math.exp(-a * dt)
+    sd = sigma * math.sqrt((1.0 - math.exp(-2.0 * a * dt)) / (2.0 * a))
+    N = book.notional / MONEY_UNIT
+
+    def body(rec: AadRecorder):
+        zeta = [rec.input(f"zero_{T:g}y", z) for T, z in zip(tenors, zeros)]
+        lam = rec.input("hazard", hazard)
+        lp_pay = []
+        for T in pay:
+            w = _curve_weights(T, tenors)
+            acc = None
+            for i in np.nonzero(w)[0]:
+                term = zeta[i].mul(float(w[i]))
+                acc = term if acc is None else acc.add(term)
+            lp_pay.append(acc)
+        surv_step = lam.mul(-dt).exp()                   # e^{-lambda dt}
+        pd_step = surv_step.neg().add(1.0)               # 1 - e^{-lambda dt}
+        x = rec.constant(0.0)
+        integ = rec.constant(0.0)
+        surv = rec.constant(1.0)
+        cva = rec.constant(0.0)
+        for k in range(1, dates + 1):
+            t = k * dt
+            x_new = x.mul(ea).add(rec.randn().mul(sd))
+            integ = integ.add(x.add(x_new).mul(0.5 * dt))
+            x = x_new
+            cw = _curve_weights(t, tenors)
+            lp = zeta[0].mul(float(cw[0]))
+            for i in range(1, len(tenors)):
+                lp = lp.add(zeta[i].mul(float(cw[i])))
+            alive = book.maturity > t + 1e-9
+            a0 = float(N[alive].sum())
+            value = rec.constant(a0)
+            for j, T in enumerate(pay):
+                live = T > t + 1e-9
+                w = 0.0
+                if live:
+                    coupon = alive & (book.maturity >= T - 1e-9)
+                    w = float((N[coupon] * book.fixed_rate[coupon]).sum() * accrual
+                              + N[alive & (np.abs(book.maturity - T) < 1e-9)].sum())
+                A = Af(t, T) if live else 0.0
+                Bn = -Bf(t, T) if live else 0.0
+                bond = lp_pay[j].sub(lp).add(x.mul(Bn).add(A)).exp()
+                value = value.sub(bond.mul(w))
+            exposure = value.max(0.0)
+            discount = lp.sub(integ).sub(0.5 * Vf(0.0, t)).exp()
+            cva = cva.add(exposure.mul(discount).mul(surv.mul(pd_step)).mul(1.0 - recovery))
+            surv = surv.mul(surv_step)
+        rec.output(cva)
+
+    return AadRecorder.record(body)
+
+
 # ---- generic tapes used by the conformance tests ---------------------------------
 
 def every_op(rec: AadRecorder) -> None:
@@ -334,4 +470,5 @@ def every_op(rec: AadRecorder) -> None:
 
 
 __all__ = ["EquityMarket", "TimeGrid", "GbmPath", "OptionType", "Barrier", "Smooth", "Products", "ExoticProducts",
-           "Inputs", "record_model", "asian_tape", "european_tape", "barrier_tape", "every_op"]
+           "Inputs", "record_model", "asian_tape", "european_tape", "barrier_tape", "every_op", "SwapBook",
+           "cva_config5_curve", "cva_tape"]

@@ -7,6 +7,8 @@ named_streams     RandomStreamsTest.cpuAndJitAgree... (RandomStreamsTest.java:66
 lookback          Products.lookback (Products.java:102-117)
 multi_output      two recorded outputs (AadRecorder.java:108-122)
 fp32_asian_50     Fp32BackendComparisonTest.asianCall (Fp32BackendComparisonTest.java:45-59)
+nonuniform_asian  an Asian call on a non-uniform TimeGrid (TimeGrid.of, TimeGrid.java): every step
+                  records its own dt and sqrt(dt) constants, so the loop's constants differ per unit
 """
 import math
 
@@ -100,3 +102,24 @@ def fp32_asian_50(fixings=50):
 def odd_steps_asian(steps=31):
     from nablatensor_b200.quant import asian_tape
     return asian_tape(steps)
+
+
+def nonuniform_asian(steps=60):
+    """Asian call on a grid whose step lengths grow geometrically: the step
+    body is the same every step except for its dt constants."""
+    w = [1.02 ** k for k in range(steps)]
+    dts = [x / sum(w) for x in w]
+
+    def body(rec):
+        spot = rec.input("spot", 100.0)
+        strike = rec.input("strike", 100.0)
+        vol = rec.input("vol", 0.2)
+        rate = rec.input("rate", 0.03)
+        drift = rate.sub(vol.mul(vol).mul(0.5))
+        s, acc = spot, rec.constant(0.0)
+        for dt in dts:
+            s = s.mul(drift.mul(dt).add(vol.mul(math.sqrt(dt)).mul(rec.randn())).exp())
+            acc = acc.add(s)
+        payoff = acc.div(float(steps)).sub(strike).max(0.0)
+        rec.output(payoff.mul(rate.neg().exp()))
+    return AadRecorder.record(body)

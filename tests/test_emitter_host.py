@@ -17,8 +17,8 @@ from nablatensor_b200 import _lib, quant
 from oracle.oracle import FlatTape
 
 from conftest import host_kernel
-from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, odd_steps_asian,
-                   random_branching)
+from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, nonuniform_asian,
+                   odd_steps_asian, random_branching)
 
 ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
 
@@ -129,6 +129,27 @@ def test_correlated_basket(oracle_mod, n, steps):
     assets, 2n + 1 inputs) at a size the host runs quickly."""
     tape = quant.basket_tape(n=n, steps=steps)
     _run(oracle_mod, tape, tape.recordedInputs(), 2_000, 5, 7)
+
+
+@pytest.mark.parametrize("steps", [60, 61])
+def test_loop_with_per_unit_constants(oracle_mod, steps):
+    """A non-uniform time grid: the steps repeat with different dt constants,
+    which the loop reads from its per-unit constant table."""
+    tape = nonuniform_asian(steps)
+    src = _run(oracle_mod, tape, [100.0, 100.0, 0.2, 0.03], 2_000, 9, 42)
+    assert "step loop" in src and "#define NT_NVARY" in src
+    dev = _lib.emit_source(tape, target=0, precision=1)
+    assert "nt_ctab" in dev and "__ldg(&nt_ctab" in dev
+
+
+def test_cva_book_is_bit_exact(oracle_mod):
+    """BASELINE config 5's shape at a size the host runs quickly: 24 monthly
+    dates over two years, 10 swaps; the per-date constants (live coupons,
+    bond coefficients, curve weights) vary from unit to unit."""
+    book = quant.SwapBook.config5(n=10)
+    tape = quant.cva_tape(dates=24, horizon=2.0, book=book)
+    src = _run(oracle_mod, tape, tape.recordedInputs(), 500, 3, 11)
+    assert "step loop: 12 units" in src and "#define NT_NVARY" in src
 
 
 def test_loop_plan_reported_for_config_tapes(ntlib):

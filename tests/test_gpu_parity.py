@@ -222,6 +222,20 @@ def test_basket_config4_fp64(engine, oracle_mod):
     _assert_parity(got, want, scale)
 
 
+def test_cva_config5_fp64(engine, oracle_mod):
+    """CVA of 100 payer swaps under Hull-White, 120 monthly
+    dates; adjoints w.r.t. the 40 pillar zero rates and the hazard rate.  The
+    loop's per-date constants come from the per-unit table."""
+    tape = quant.cva_tape()
+    assert tape.input_count() == 41
+    with engine.compile(tape, FP64) as ex:
+        info = ex.info()
+        assert info["loop_units"] == 60 and info["loop_unit"] == 686
+        got, _ = ex.replay_sums(20_000, 0x1_0000_0003, 11)
+    want, scale = _oracle(oracle_mod, tape, tape.recordedInputs(), 20_000, 0x1_0000_0003, 11)
+    _assert_parity(got, want, scale)
+
+
 @pytest.mark.parametrize("make,base,f32", [
     (lambda: quant.asian_tape(252), ATM, False),
     (lambda: quant.barrier_tape(252), ATM, True),
