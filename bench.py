@@ -193,7 +193,7 @@ def run_reference(args, rank: int, wl: Workload) -> None:
                                    f"timed: C restatement of its scalar `cpu` engine"},
         "e2e": {"value": value, "unit": "scenarios/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None:
@@ -284,23 +284,36 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
     # launches at boost clock) and the sustained rate (3 s of back-to-back
     # launches under the 1 kW power limit).  A timed region longer than a
     # second runs power-limited, so its denominator is the sustained figure.
-    peak_burst = _lib.fma_peak(local_rank, not wl.f32)
-    peak_sus = _lib.fma_peak_sustained(local_rank, not wl.f32, 3000)
     long_run = my_total_ms > 1000.0
-    peak = peak_sus if long_run else peak_burst
+    peaks = {}
+    for fp64 in ((True, False) if wl.f32 else (True,)):
+        burst = _lib.fma_peak(local_rank, fp64)
+        sus = _lib.fma_peak_sustained(local_rank, fp64, 3000)
+        peaks["fp64" if fp64 else "fp32"] = (sus if long_run else burst, burst, sus)
     flops_per_scen = info["fwd_flops"] + info["rev_flops"]
     kernel_s = (my_total_ms * 1e-3) / (args.steps * launches_per_step)
     paths_per_launch = mine / launches_per_step
-    achieved = flops_per_scen * paths_per_launch / kernel_s / 1e12
-    pipe = "FFMA" if wl.f32 else "DFMA"
-    roofline = {"bound": wl.dtype.replace("f", "fp"), "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+    # The pipe that bounds the kernel.  An fp32 tape under the reference's
+    # fp32 semantics evaluates exp, log and Box-Muller in fp64 (wide_flops);
+    # its bound is whichever pipe needs longer for its share of the flops.
+    split = {"fp64": flops_per_scen}
+    if wl.f32:
+        split = {"fp64": info["wide_flops"], "fp32": flops_per_scen - info["wide_flops"]}
+    bound = max(split, key=lambda k: split[k] / peaks[k][0])
+    peak, peak_burst, peak_sus = peaks[bound]
+    achieved = split[bound] * paths_per_launch / kernel_s / 1e12
+    pipe = "DFMA" if bound == "fp64" else "FFMA"
+    roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak,
                 "peak_source": (f"measured {pipe} rate on this GPU, of measured: "
                                 + ("sustained over 3 s under the power limit (nt_fma_peak_sustained), the "
                                    "timed region being longer than 1 s" if long_run else
                                    "burst (nt_fma_peak), the timed region being shorter than 1 s")),
                 "peak_burst": peak_burst, "peak_sustained": peak_sus, "frac_of_burst": achieved / peak_burst,
-                "flops_per_scenario": flops_per_scen, "traffic": _profiled_traffic(wl, paths_per_launch)}
+                "flops_per_scenario": split[bound], "traffic": _profiled_traffic(wl, paths_per_launch)}
+    if wl.f32:
+        roofline["flops_split"] = {k: {"flops_per_scenario": v, "frac": v * paths_per_launch / kernel_s / 1e12 /
+                                       peaks[k][0]} for k, v in split.items()}
 
     line = None
     if rank == 0:
@@ -327,7 +340,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
         dist.destroy_process_group()
     ex.close()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def _profiled_traffic(wl: Workload, paths_per_launch: float):
@@ -343,11 +356,26 @@ def _profiled_traffic(wl: Workload, paths_per_launch: float):
     return None
 
 
+_RESULT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    """The one JSON line, on the process's real stdout."""
+    _RESULT.write(json.dumps(line) + "\n")
+    _RESULT.flush()
+
+
 def main():
-    # NCCL prints a version banner on stdout when a communicator is set up
-    # (NCCL_DEBUG unset or VERSION); stdout carries exactly one JSON line.
+    global _RESULT
+    # stdout carries exactly one JSON line.  Native libraries (NCCL's version
+    # banner at communicator set-up, for one) write to file descriptor 1
+    # directly, so descriptor 1 goes to stderr for the whole run and the
+    # result is written to a duplicate of the original stdout.
     if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
         os.environ["NCCL_DEBUG"] = "WARN"
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)

@@ -142,6 +142,8 @@ typedef struct nt_exec_info {
   double compile_seconds;   /* NVRTC + module load, 0 on a cache hit */
   double fwd_flops;         /* algorithmic flops per scenario, forward (weights in DESIGN) */
   double rev_flops;         /* algorithmic flops per scenario, reverse */
+  double wide_flops;        /* fp32 tapes: the part of fwd_flops evaluated in fp64 (exp, log and
+                               Box-Muller under the reference's fp32 semantics); 0 for fp64 tapes */
 } nt_exec_info;
 
 /* ABI version (NT_ABI_VERSION of the built library). */

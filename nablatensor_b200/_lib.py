@@ -62,7 +62,8 @@ class NtExecInfo(ctypes.Structure):
         "channels", "loop_start", "loop_unit", "loop_units", "steps_per_unit", "seg_units", "segments",
         "ckpt_slots", "stored_per_unit", "ckpt_global", "tape_slots", "tape_mbytes", "markets_registers",
         "markets_local_bytes")] + [
-        ("compile_seconds", ctypes.c_double), ("fwd_flops", ctypes.c_double), ("rev_flops", ctypes.c_double)]
+        ("compile_seconds", ctypes.c_double), ("fwd_flops", ctypes.c_double), ("rev_flops", ctypes.c_double),
+        ("wide_flops", ctypes.c_double)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}

@@ -256,6 +256,7 @@ void Exec::load(int max_regs) {
   info.compile_seconds = compile_seconds;
   info.fwd_flops = plan.fwd_flops;
   info.rev_flops = plan.rev_flops;
+  info.wide_flops = plan.wide_flops;
 }
 
 Exec::~Exec() {

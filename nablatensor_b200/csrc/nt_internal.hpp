@@ -94,6 +94,7 @@ struct Plan {
   Loop loop;
   double fwd_flops = 0.0;  // algorithmic, per scenario
   double rev_flops = 0.0;
+  double wide_flops = 0.0;  // of fwd_flops: what an fp32 tape evaluates in fp64 (reference fp32 semantics)
   int32_t stored_per_unit = 0;
   int32_t per_unit_regs = 0;  // registers one loop unit's reverse values take (estimate)
 };

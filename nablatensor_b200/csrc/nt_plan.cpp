@@ -487,9 +487,15 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
   w.log = kFlopWeights[1];
   w.sqrt = kFlopWeights[2];
   w.sincos = kFlopWeights[3];
-  double fwd = 0, rev = 0;
+  double fwd = 0, rev = 0, wide = 0;
   for (int32_t i = 0; i < t.n; ++i) {
     const int op = t.op[i];
+    // fp32 under the reference's semantics: exp, log and Box-Muller run in fp64.
+    if (cfg.f32 && cfg.wide32) {
+      if (op == NT_EXP) wide += w.exp;
+      else if (op == NT_LOG) wide += w.log;
+      else if (op == NT_RANDN) wide += 0.5 * (w.log + w.sqrt + w.sincos + 8.0);
+    }
     switch (op) {
       case NT_ADD: case NT_SUB: fwd += w.add; break;
       case NT_MUL: fwd += w.mul; break;
@@ -524,6 +530,7 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     }
   }
   p.fwd_flops = fwd;
+  p.wide_flops = wide;
   p.rev_flops = cfg.adjoints ? rev * t.n_out() : 0.0;
   return p;
 }
