@@ -123,6 +123,12 @@ class Emitter {
     return "d" + std::to_string(x);
   }
   bool active_outside(int32_t x) const { return in_loop(x) ? lp_.body[lp_.off(x)].active : t_.active[x] != 0; }
+  // A gathered argument is active when any unit's node is.
+  bool gather_active(int32_t k) const {
+    for (int32_t x : lp_.gather[k])
+      if (t_.active[x]) return true;
+    return false;
+  }
 
   std::string fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a) const;
   void emit_straight_forward(int32_t lo, int32_t hi);
@@ -281,6 +287,7 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
       if (g == 0) return "cs" + std::to_string(r.idx);
       return "r" + std::to_string(g - 1) + "_" + std::to_string(r.idx);
     }
+    if (r.kind == REF_GATHER) return "nt_gv" + std::to_string(r.idx) + "[" + unit + "]";
     return val_outside(r.idx);
   };
   // Pairing of normal draws inside the unit.
@@ -348,17 +355,20 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
 void Emitter::emit_body_reverse(int g) {
   const int32_t L = lp_.L;
   const std::string G = std::to_string(g);
+  const std::string unit = "(s * " + std::to_string(lp_.G) + " + " + G + ")";
   auto val = [&](const Ref& r) -> std::string {
     if (r.kind == REF_SAME) return "r" + G + "_" + std::to_string(r.idx);
     if (r.kind == REF_CARRY) {
       if (g == 0) return "cs" + std::to_string(r.idx);
       return "r" + std::to_string(g - 1) + "_" + std::to_string(r.idx);
     }
+    if (r.kind == REF_GATHER) return "nt_gv" + std::to_string(r.idx) + "[" + unit + "]";
     return val_outside(r.idx);
   };
   auto adj = [&](const Ref& r, bool* active) -> std::string {
     if (r.kind == REF_SAME) { *active = lp_.body[r.idx].active; return "b" + std::to_string(r.idx); }
     if (r.kind == REF_CARRY) { *active = lp_.body[r.idx].active; return "n" + std::to_string(r.idx); }
+    if (r.kind == REF_GATHER) { *active = gather_active(r.idx); return "nt_gd" + std::to_string(r.idx) + "[" + unit + "]"; }
     *active = t_.active[r.idx] != 0;
     return "d" + std::to_string(r.idx);
   };
@@ -433,6 +443,9 @@ void Emitter::emit_reverse_for_output(int o) {
     zero_.clear();  // the segment loop runs its code more than once
     const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
     const int32_t nck = (int32_t)lp_.ckpt.size();
+    for (size_t k = 0; k < lp_.gather.size(); ++k)
+      if (gather_active((int32_t)k))
+        o_.line("real nt_gd" + std::to_string(k) + "[" + std::to_string(lp_.N) + "] = {};");
     o_.open("for (int s = " + std::to_string(K - 1) + "; s >= 0; --s) {");
     for (int32_t c = 0; c < nck; ++c)
       o_.line("const real cs" + std::to_string(lp_.ckpt[c]) + " = NT_CK(s * " + std::to_string(nck) + " + " +
@@ -468,6 +481,14 @@ void Emitter::emit_reverse_for_output(int o) {
       const int32_t k = lp_.carries[c], x = lp_.carry_init[c];
       if (lp_.body[k].active && t_.active[x]) o_.line("d" + std::to_string(x) + " += cd" + std::to_string(k) + ";");
     }
+    // Each unit's gathered adjoint belongs to the node that unit read (last
+    // unit first, the order in which the interpreter would have added them).
+    for (size_t k = 0; k < lp_.gather.size(); ++k)
+      if (gather_active((int32_t)k))
+        for (int32_t u = lp_.N - 1; u >= 0; --u)
+          if (t_.active[lp_.gather[k][u]])
+            o_.line("d" + std::to_string(lp_.gather[k][u]) + " += nt_gd" + std::to_string(k) + "[" + std::to_string(u) +
+                    "];");
     emit_straight_reverse(0, lp_.B);
   }
   for (int32_t j = 0; j < t_.n_in(); ++j) {
@@ -502,6 +523,13 @@ void Emitter::emit_scenario() {
   } else {
     const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
     emit_straight_forward(0, lp_.B);
+    // Gathered arguments: the prologue node each unit reads, as one array
+    // indexed by the unit.
+    for (size_t k = 0; k < lp_.gather.size(); ++k) {
+      std::string init;
+      for (int32_t x : lp_.gather[k]) init += (init.empty() ? "" : ", ") + val_outside(x);
+      o_.line("const real nt_gv" + std::to_string(k) + "[" + std::to_string(lp_.N) + "] = {" + init + "};");
+    }
     o_.line("// step loop: " + std::to_string(lp_.N) + " units of " + std::to_string(L) + " nodes (" +
             std::to_string(lp_.steps_per_unit) + " steps each), " + std::to_string(K) + " segments of " +
             std::to_string(G) + " units");

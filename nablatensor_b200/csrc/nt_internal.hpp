@@ -46,7 +46,10 @@ struct Tape {
 Tape ingest(const nt_tape* t);
 
 // How a loop-body argument is reached.
-enum RefKind : int8_t { REF_NONE = 0, REF_SAME = 1, REF_CARRY = 2, REF_OUT = 3 };
+// An argument of a loop unit: the same unit, the previous unit (a carry), one
+// fixed node before the loop (an invariant), or a node before the loop that
+// changes from unit to unit (gathered through Loop::gather[idx]).
+enum RefKind : int8_t { REF_NONE = 0, REF_SAME = 1, REF_CARRY = 2, REF_OUT = 3, REF_GATHER = 4 };
 struct Ref {
   RefKind kind = REF_NONE;
   int32_t idx = -1;  // SAME/CARRY: offset in the unit; OUT: node index outside the loop
@@ -80,6 +83,7 @@ struct Loop {
   std::vector<uint8_t> recompute;   // per offset: recomputed from the segment checkpoint
   std::vector<int32_t> tape_slot;   // per offset: slot in the per-thread value tape, or -1
   int32_t n_tape = 0;               // taped values per unit
+  std::vector<std::vector<int32_t>> gather;  // per REF_GATHER slot: the node each unit reads
   int32_t n_vary = 0;               // CONST offsets whose value differs between units
   std::vector<double> ctab;         // their values, [unit][cslot] (a non-uniform time grid, date tables)
   int32_t G = 0;                    // units per segment

@@ -43,7 +43,9 @@ bool compat(const Tape& t, int32_t i, int32_t L) {
   if (is_draw(op)) return t.b[i] == t.b[j] && t.a[j] > t.a[i];
   for (int w = 0; w < nargs(op); ++w) {
     const int32_t x = arg(t, i, w), y = arg(t, j, w);
-    if (y != x + L && y != x) return false;
+    // shifted with the unit, the same node, or two nodes before the unit
+    // (a per-unit gathered value; validate() checks they precede the loop)
+    if (y != x + L && y != x && !(x < i - L && y < i)) return false;
   }
   return true;
 }
@@ -80,8 +82,8 @@ int32_t validate(const Tape& t, int32_t B, int32_t L, int32_t* ncarries) {
         if (init[r.idx] < 0) init[r.idx] = x0;
         else if (init[r.idx] != x0) return 0;
       } else {
-        r = {REF_OUT, x1};
-        if (x0 != x1) return 0;
+        // before the loop: one invariant node, or a different node per unit
+        r = {x0 == x1 ? REF_OUT : REF_GATHER, x1};
       }
       (w == 0 ? ra : rb)[j] = r;
     }
@@ -106,6 +108,7 @@ int32_t validate(const Tape& t, int32_t B, int32_t L, int32_t* ncarries) {
         const int32_t x = arg(t, i, w);
         if (r.kind == REF_SAME) ok = x == (int32_t)base + r.idx;
         else if (r.kind == REF_CARRY) ok = x == (int32_t)(base - L) + r.idx;
+        else if (r.kind == REF_GATHER) ok = x < B;
         else ok = x == r.idx;
       }
     }
@@ -159,8 +162,13 @@ std::vector<int32_t> candidate_periods(const Tape& t) {
 
 Candidate find_loop(const Tape& t) {
   Candidate best;
+  std::vector<int32_t> found;  // periods that gave a loop
   for (int32_t L : candidate_periods(t)) {
     if (3 * (int64_t)L > t.n) continue;
+    // A multiple of a period that already gave a loop only folds its units.
+    bool multiple = false;
+    for (int32_t f : found) multiple |= L % f == 0;
+    if (multiple) continue;
     // Longest strict run of compat(i, L).
     int32_t run_s = -1, run_len = 0, cur_s = -1, cur_len = 0;
     for (int32_t i = 0; i + L < t.n; ++i) {
@@ -173,13 +181,21 @@ Candidate find_loop(const Tape& t) {
       }
     }
     if (run_len < 2 * L) continue;
+    // Every rotation of a periodic body validates, each at a cost of the whole
+    // loop: a long unit is tried only at the starts that are draws (and the
+    // run's own start), a short one at every start.
+    const bool long_unit = L > 64;
+    bool any = false;
     for (int32_t B = std::max(0, run_s - 2 * L); B <= run_s; ++B) {
+      if (long_unit && B != run_s && !is_draw(t.op[B])) continue;
       int32_t carries = 0;
       const int32_t N = validate(t, B, L, &carries);
       if (N < 3) continue;
+      any = true;
       const int64_t cover = (int64_t)N * L, bcover = (int64_t)best.N * best.L;
       if (cover > bcover || (cover == bcover && carries < best.carries)) best = {B, L, N, carries};
     }
+    if (any) found.push_back(L);
   }
   return best;
 }
@@ -188,6 +204,7 @@ Candidate find_loop(const Tape& t) {
 void describe(const Tape& t, Loop& lp) {
   const int32_t B = lp.B, L = lp.L, N = lp.N;
   lp.body.assign(L, BodyNode{});
+  lp.gather.clear();
   lp.is_carry.assign(L, 0);
   lp.carry_slot.assign(L, -1);
   lp.is_exit.assign(L, 0);
@@ -207,7 +224,23 @@ void describe(const Tape& t, Loop& lp) {
       Ref r;
       if (x1 >= B + L) r = {REF_SAME, x1 - (B + L)};
       else if (x1 >= B) { r = {REF_CARRY, x1 - B}; init[r.idx] = x0; lp.is_carry[r.idx] = 1; }
-      else r = {REF_OUT, x1};
+      else if (x0 == x1) r = {REF_OUT, x1};
+      else {
+        // A different node before the loop in each unit.  Arguments that read
+        // the same node in every unit share one slot, so that node's adjoint
+        // collects its unit's contributions in one place, in the reverse
+        // sweep's order.
+        std::vector<int32_t> nodes(N);
+        for (int32_t u = 0; u < N; ++u) nodes[u] = arg(t, B + u * L + j, w);
+        int32_t slot = -1;
+        for (size_t k = 0; k < lp.gather.size() && slot < 0; ++k)
+          if (lp.gather[k] == nodes) slot = (int32_t)k;
+        if (slot < 0) {
+          slot = (int32_t)lp.gather.size();
+          lp.gather.push_back(std::move(nodes));
+        }
+        r = {REF_GATHER, slot};
+      }
       (w == 0 ? bn.ra : bn.rb) = r;
     }
     uint8_t act = 0;

@@ -331,7 +331,7 @@ def barrier_tape(steps: int = 252, level: float = 80.0, width: float = 1.0, kind
 #
 #   x_k   = x_{k-1} e^{-a dt} + sigma sqrt((1 - e^{-2a dt}) / 2a) z_k   (exact OU step)
 #   I_k   = I_{k-1} + (x_{k-1} + x_k) dt / 2                           (integral of x)
-#   lp_k  = ln P(0, t_k) = sum_i C_ki zeta_i                          (zero rates zeta_i at the pillars)
+#   lp_k  = ln P(0, t_k), from the two pillar zero rates around t_k    (before the loop, gathered per date)
 #   P_kj  = P(t_k, T_j) = exp(lp(T_j) - lp_k + A(t_k, T_j) - B(t_k, T_j) x_k)
 #   V_k   = A0_k - sum_j W_kj P_kj                                     (netted payer value, in millions)
 #   D_k   = exp(lp_k - I_k - V(0, t_k) / 2)                              (stochastic discount)
@@ -415,6 +415,16 @@ def cva_tape(dates: int = 120, horizon: float = 10.0, a: float = 0.05, sigma: fl
                 term = zeta[i].mul(float(w[i]))
                 acc = term if acc is None else acc.add(term)
             lp_pay.append(acc)
+        # ln P(0, t_k) of every exposure date, before the loop: each date's
+        # body reads its own (the loop gathers them per unit).
+        lp_dates = []
+        for k in range(1, dates + 1):
+            w = _curve_weights(k * dt, tenors)
+            acc = None
+            for i in np.nonzero(w)[0]:
+                term = zeta[i].mul(float(w[i]))
+                acc = term if acc is None else acc.add(term)
+            lp_dates.append(acc)
         surv_step = lam.mul(-dt).exp()                   # e^{-lambda dt}
         pd_step = surv_step.neg().add(1.0)               # 1 - e^{-lambda dt}
         x = rec.constant(0.0)
@@ -426,10 +436,7 @@ def cva_tape(dates: int = 120, horizon: float = 10.0, a: float = 0.05, sigma: fl
             x_new = x.mul(ea).add(rec.randn().mul(sd))
             integ = integ.add(x.add(x_new).mul(0.5 * dt))
             x = x_new
-            cw = _curve_weights(t, tenors)
-            lp = zeta[0].mul(float(cw[0]))
-            for i in range(1, len(tenors)):
-                lp = lp.add(zeta[i].mul(float(cw[i])))
+            lp = lp_dates[k - 1]
             alive = book.maturity > t + 1e-9
             a0 = float(N[alive].sum())
             value = rec.constant(a0)

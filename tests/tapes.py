@@ -9,6 +9,8 @@ multi_output      two recorded outputs (AadRecorder.java:108-122)
 fp32_asian_50     Fp32BackendComparisonTest.asianCall (Fp32BackendComparisonTest.java:45-59)
 nonuniform_asian  an Asian call on a non-uniform TimeGrid (TimeGrid.of, TimeGrid.java): every step
                   records its own dt and sqrt(dt) constants, so the loop's constants differ per unit
+term_vol_asian    an Asian call with a volatility input per step: every step reads its own input and
+                  its own drift node from before the loop (gathered per unit)
 """
 import math
 
@@ -119,6 +121,26 @@ def nonuniform_asian(steps=60):
         s, acc = spot, rec.constant(0.0)
         for dt in dts:
             s = s.mul(drift.mul(dt).add(vol.mul(math.sqrt(dt)).mul(rec.randn())).exp())
+            acc = acc.add(s)
+        payoff = acc.div(float(steps)).sub(strike).max(0.0)
+        rec.output(payoff.mul(rate.neg().exp()))
+    return AadRecorder.record(body)
+
+
+def term_vol_asian(steps=24):
+    """Asian call with a term structure of volatility: step k reads input
+    vol_k and a drift computed for it before the loop."""
+    dt = 1.0 / steps
+
+    def body(rec):
+        spot = rec.input("spot", 100.0)
+        strike = rec.input("strike", 100.0)
+        rate = rec.input("rate", 0.03)
+        vols = [rec.input(f"vol_{k}", 0.15 + 0.2 * k / steps) for k in range(steps)]
+        drifts = [rate.sub(v.mul(v).mul(0.5)).mul(dt) for v in vols]
+        s, acc = spot, rec.constant(0.0)
+        for k in range(steps):
+            s = s.mul(drifts[k].add(vols[k].mul(math.sqrt(dt)).mul(rec.randn())).exp())
             acc = acc.add(s)
         payoff = acc.div(float(steps)).sub(strike).max(0.0)
         rec.output(payoff.mul(rate.neg().exp()))

@@ -18,7 +18,7 @@ from oracle.oracle import FlatTape
 
 from conftest import host_kernel
 from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, nonuniform_asian,
-                   odd_steps_asian, random_branching)
+                   odd_steps_asian, random_branching, term_vol_asian)
 
 ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
 
@@ -140,6 +140,15 @@ def test_loop_with_per_unit_constants(oracle_mod, steps):
     assert "step loop" in src and "#define NT_NVARY" in src
     dev = _lib.emit_source(tape, target=0, precision=1)
     assert "nt_ctab" in dev and "__ldg(&nt_ctab" in dev
+
+
+@pytest.mark.parametrize("steps", [24, 25])
+def test_loop_with_gathered_inputs(oracle_mod, steps):
+    """A volatility per step: each unit reads its own input and its own drift
+    node from before the loop, and their adjoints flow back to those nodes."""
+    tape = term_vol_asian(steps)
+    src = _run(oracle_mod, tape, tape.recordedInputs(), 2_000, 9, 42)
+    assert "step loop" in src and "nt_gv0" in src and "nt_gd0" in src
 
 
 def test_cva_book_is_bit_exact(oracle_mod):
