@@ -314,6 +314,16 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
       continue;
     }
     const std::string key = "key" + std::to_string(bn.stream);
+    if (bn.op == NT_RANDN && !recompute && lp_.half_pairs && (bn.draw_stride & 1)) {
+      // Units alternate: an even ordinal draws the pair, the next unit takes
+      // the kept second leg (the loop starts at an even ordinal).
+      const std::string ord = "(nt_u32)(" + std::to_string(bn.draw_base) + " + " + unit + " * " +
+                              std::to_string(bn.draw_stride) + ")";
+      o_.line("if ((" + ord + " & 1u) == 0u) " + rng_pair() + key + ", " + ord + " >> 1, &" + name(j) +
+              ", &nt_hl" + std::to_string(j) + "); else " + name(j) + " = nt_hl" + std::to_string(j) + ";");
+      emitted[j] = 1;
+      continue;
+    }
     if (bn.op == NT_RANDN) {
       auto it = partner.find(j);
       if (it != partner.end()) {
@@ -535,6 +545,11 @@ void Emitter::emit_scenario() {
             std::to_string(G) + " units");
     for (size_t c = 0; c < lp_.carries.size(); ++c)
       o_.line("real cv" + std::to_string(lp_.carries[c]) + " = " + val_outside(lp_.carry_init[c]) + ";");
+    if (lp_.half_pairs)
+      for (int32_t j = 0; j < L; ++j)
+        if (lp_.body[j].op == NT_RANDN && (lp_.body[j].draw_stride & 1))
+          o_.line("real nt_hl" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;") +
+                  "  // second Box-Muller leg, kept for the next unit");
     for (int32_t j : lp_.exits)
       if (!lp_.is_carry[j]) o_.line("real xv" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
     const int32_t nck = (int32_t)lp_.ckpt.size();
@@ -708,7 +723,13 @@ std::string Emitter::run() {
   }
   o_.line("#define NT_NLOOP " + std::to_string(lp_.present ? lp_.N : 0));
   o_.line("#define NT_TAPE(u, slot) nt_tape_b[((u) * NT_NTAPE + (slot)) * NT_BLOCK]");
-  std::string bounds = "__launch_bounds__(NT_BLOCK" + (cfg_.min_blocks > 0 ? ", " + std::to_string(cfg_.min_blocks) : std::string()) + ")";
+  // Launch bounds size the register budget for NT_BLOCK threads (and
+  // min_blocks resident blocks); an explicit cap replaces them (NVRTC ignores
+  // --maxrregcount on a kernel that has launch bounds).
+  std::string bounds = cfg_.max_regs > 0
+                           ? "__maxnreg__(" + std::to_string(cfg_.max_regs) + ")"
+                           : "__launch_bounds__(NT_BLOCK" +
+                                 (cfg_.min_blocks > 0 ? ", " + std::to_string(cfg_.min_blocks) : std::string()) + ")";
   if (mk) {
     o_.line("extern \"C\" __global__ void " + bounds + " nt_markets_kernel(");
     o_.line("    const double* __restrict__ inputs, int n_states, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");

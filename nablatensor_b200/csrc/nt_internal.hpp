@@ -71,6 +71,9 @@ struct Loop {
   bool present = false;
   int32_t B = -1, L = 0, N = 0;
   int32_t steps_per_unit = 1;  // tape iterations folded into one unit (RNG pairing)
+  // A long unit with one normal per stream and stride 1 is not folded: an even
+  // unit draws the Box-Muller pair and keeps the second leg for the next unit.
+  bool half_pairs = false;
   std::vector<BodyNode> body;
   std::vector<int32_t> carries;     // unit offsets read by the next unit
   std::vector<int32_t> carry_init;  // per carry: the node feeding unit 0
@@ -118,6 +121,7 @@ struct EmitConfig {
   int32_t fwd_unroll = 1;  // unroll of the forward unit loop
   int32_t block = 128;
   int32_t min_blocks = 0;
+  int32_t max_regs = 0;    // register cap (__maxnreg__; launch bounds would override --maxrregcount)
   int32_t seg_units = 0;   // 0 = automatic
   int32_t target = 0;      // 0 CUDA, 1 host C++
   // Multi-market variant: one launch replays every scenario under n_states

@@ -338,6 +338,8 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   if (opt->max_regs != 0 && (opt->max_regs < 32 || opt->max_regs > 255))
     fail(NT_E_INVALID_ARG, "max_regs must be 0 or in [32, 255]");
   cfg.min_blocks = opt->min_blocks;
+  cfg.max_regs = opt->max_regs;
+  if (cfg.max_regs > 0 && cfg.min_blocks > 0) fail(NT_E_INVALID_ARG, "max_regs and min_blocks are exclusive");
   cfg.seg_units = opt->seg_units;
   cfg.target = target;
   if (opt->fwd_unroll < 0 || opt->fwd_unroll > 16) fail(NT_E_INVALID_ARG, "fwd_unroll must be in [0, 16]");
@@ -378,10 +380,18 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
     // Fold iterations so each unit draws whole Box-Muller pairs: a pair's two
     // legs must land in the same unit and start at an even ordinal.
     describe(t, lp);
-    bool odd_stride = false, odd_base = false;
+    bool odd_stride = false, odd_base = false, single_draws = true;
+    std::map<int32_t, int32_t> per_stream;
     for (const BodyNode& bn : lp.body)
-      if (bn.op == NT_RANDN) odd_stride |= (bn.draw_stride & 1) != 0;
-    int32_t U = odd_stride ? 2 : 1;
+      if (bn.op == NT_RANDN) {
+        odd_stride |= (bn.draw_stride & 1) != 0;
+        single_draws &= bn.draw_stride == 1 && ++per_stream[bn.stream] == 1;
+      }
+    // A long unit keeps its recorded length and carries the second Box-Muller
+    // leg from an even unit to the next (fewer values live in a unit's
+    // reverse sweep); a short one is folded in pairs.
+    const bool half = odd_stride && single_draws && lp.L > 128;
+    int32_t U = (odd_stride && !half) ? 2 : 1;
     // Smallest normal ordinal per stream in unit 0.
     std::map<int32_t, int32_t> first;
     for (const BodyNode& bn : lp.body)
@@ -441,6 +451,7 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
         describe(t, lp);
         lp.G = G;
         lp.K = K;
+        lp.half_pairs = half;
       }
     }
   }

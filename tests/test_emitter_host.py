@@ -161,6 +161,16 @@ def test_cva_book_is_bit_exact(oracle_mod):
     assert "step loop: 12 units" in src and "#define NT_NVARY" in src
 
 
+@pytest.mark.parametrize("flags", [0, _lib.NT_FLAG_RECOMPUTE_ALL])
+def test_cva_config5_carries_the_second_leg(oracle_mod, flags):
+    """The full config-5 tape: one long unit per monthly date drawing one
+    normal, so an even unit draws the Box-Muller pair and the next unit takes
+    the kept second leg (recompute-all regenerates single draws instead)."""
+    tape = quant.cva_tape()
+    src = _run(oracle_mod, tape, tape.recordedInputs(), 40, 0x1_0000_0003, 11, flags=flags)
+    assert "units of 224 nodes (1 steps each)" in src and "nt_hl" in src
+
+
 def test_loop_plan_reported_for_config_tapes(ntlib):
     src = _lib.emit_source(quant.barrier_tape(252), target=0, precision=0)
     assert "step loop: 126 units of 32 nodes (2 steps each)" in src

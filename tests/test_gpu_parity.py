@@ -231,7 +231,7 @@ def test_cva_config5_fp64(engine, oracle_mod):
     assert tape.input_count() == 41
     with engine.compile(tape, FP64) as ex:
         info = ex.info()
-        assert info["loop_units"] >= 59 and info["loop_unit"] == 448  # two dates per unit
+        assert info["loop_units"] >= 118 and info["loop_unit"] == 224  # one date per unit
         got, _ = ex.replay_sums(20_000, 0x1_0000_0003, 11)
     want, scale = _oracle(oracle_mod, tape, tape.recordedInputs(), 20_000, 0x1_0000_0003, 11)
     _assert_parity(got, want, scale)

@@ -74,7 +74,7 @@ def test_noalloc_rejects_an_executable_with_global_scratch(ntlib):
 
 def test_noalloc_rejects_scratch_beyond_the_maximum(ntlib):
     import torch
-    n_in = 300  # 302 channels: the reduction records of a full grid exceed 1 MiB
+    n_in = 300  # 302 channels; with 32-thread blocks a full grid's reduction records exceed 1 MiB
 
     def body(rec):
         xs = [rec.input(f"x{j}", 1.0 + j) for j in range(n_in)]
@@ -84,8 +84,9 @@ def test_noalloc_rejects_scratch_beyond_the_maximum(ntlib):
         rec.output(acc)
 
     tape = AadRecorder.record(body)
-    ex = B200AadExecutable(tape, FP64, 0, flags=NOALLOC_FLAGS)
+    ex = B200AadExecutable(tape, FP64.with_engine_option("cuda", "block", "32"), 0, flags=NOALLOC_FLAGS)
     try:
+        assert ex.info()["grid"] * (2 + n_in) * 8 > (1 << 20)
         d_in = torch.ones(n_in, dtype=torch.float64, device="cuda:0")
         d_sums = torch.zeros(2 + n_in, dtype=torch.float64, device="cuda:0")
         rc = _noalloc(ex, 10_000_000, 0, 1, d_in, d_sums, torch.cuda.current_stream(0))
