@@ -173,6 +173,7 @@ Exec* Exec::create(const nt_tape* tape, const nt_options* opt) {
   x->source = emit(x->tape, x->plan, x->cfg);
   x->inputs.assign(x->tape.n_in(), 0.0);
   for (int32_t j = 0; j < x->tape.n_in(); ++j) x->inputs[j] = tape->constant[x->tape.input_node[j]];
+  x->auto_regs = opt->max_regs == 0 && opt->min_blocks == 0;
   x->load(opt->max_regs);
   return x.release();
 }
@@ -201,6 +202,25 @@ void Exec::load(int max_regs) {
              "cuFuncSetAttribute");
   int regs = 0, local = 0, ssm = 0;
   cu_check(d.funcGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, function), "cuFuncGetAttribute");
+  if (auto_regs && regs >= 255) {
+    // The register file ran out: the kernel spills at any occupancy, and a
+    // latency-bound sweep gains more from twice the resident warps than it
+    // loses to further spills (a 118-unit CVA book: +56 %).  Recompile with
+    // a cap of 128 registers.
+    double secs2 = 0.0;
+    cfg.max_regs = 128;
+    source = emit(tape, plan, cfg);
+    std::vector<char> capped = nvrtc_compile(source, "sm_100a", use_disk_cache, &secs2, cfg.fmad, max_regs);
+    secs += secs2;
+    cu_check(d.moduleUnload(module), "cuModuleUnload");
+    module = nullptr;
+    cu_check(d.moduleLoadData(&module, capped.data()), "cuModuleLoadData");
+    cu_check(d.moduleGetFunction(&function, module, "nt_replay_kernel"), "cuModuleGetFunction");
+    if (dyn_smem > 0)
+      cu_check(d.funcSetAttribute(function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_smem),
+               "cuFuncSetAttribute");
+    cu_check(d.funcGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, function), "cuFuncGetAttribute");
+  }
   cu_check(d.funcGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, function), "cuFuncGetAttribute");
   cu_check(d.funcGetAttribute(&ssm, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, function), "cuFuncGetAttribute");
   int per_sm = 0;
