@@ -306,20 +306,33 @@ NT_FN double nt_exp64w(double x, unsigned lanes, bool& wide) {
 }
 #endif
 
+#ifndef NT_HOST
+/* The forward loop's form of an exp the reverse sweep recomputes: the bare
+ * series, with a wide argument recorded in `wide`.  A warp in which any lane
+ * recorded one runs the loop again with nt_exp64w (the emitted kernel's redo
+ * pass), so the series is only ever kept where it is accurate. */
+NT_FN double nt_exp_series_flag(double x, bool& wide) {
+  wide |= !(fabs(x) <= 0.125);
+  return nt_exp_small(x);
+}
+#endif
+
 /* EXP nodes of fp64 tapes: the dedicated routine on the device (the emitted
  * kernel declares nt_lanes = __activemask() and nt_wide at the top of each
  * scenario), libm in the host build (bit-for-bit with the oracle).
- * NT_EXP64W is the forward sweep's form for a loop exp the reverse sweep
- * recomputes (it records wide arguments in nt_wide); NT_EXP64_SERIES is that
- * recompute once the forward sweep has shown every argument of the warp in the
- * series range. */
+ * NT_EXP64F is the forward loop's form for an exp the reverse sweep recomputes
+ * (the bare series, wide arguments recorded in nt_wide), NT_EXP64W the redo
+ * pass's (guarded, recording too); NT_EXP64_SERIES is the recompute once the
+ * forward sweep has shown every argument of the warp in the series range. */
 #ifdef NT_HOST
 #define NT_EXP64(x) exp(x)
 #define NT_EXP64W(x) exp(x)
+#define NT_EXP64F(x) exp(x)
 #define NT_EXP64_SERIES(x) exp(x)
 #else
 #define NT_EXP64(x) nt_exp64m((x), nt_lanes)
 #define NT_EXP64W(x) nt_exp64w((x), nt_lanes, nt_wide)
+#define NT_EXP64F(x) nt_exp_series_flag((x), nt_wide)
 #define NT_EXP64_SERIES(x) nt_exp_small(x)
 #endif
 

@@ -90,8 +90,11 @@ class Emitter {
   // Reverse-sweep copy for warps whose forward exps all stayed in the series
   // range: recomputed EXP nodes use the bare series (no per-node branch).
   bool series_exp_ = false;
-  // The fp64 exp form fwd_expr emits (NT_EXP64, NT_EXP64W or NT_EXP64_SERIES).
+  // The fp64 exp form fwd_expr emits (NT_EXP64, NT_EXP64W, NT_EXP64F or
+  // NT_EXP64_SERIES).
   std::string exp_fn_ = "NT_EXP64(";
+  // Forward loop pass that evaluates the recomputed exps by the bare series.
+  bool fwd_fast_ = false;
   std::string contrib(const std::string& x, char sign, const std::string& e) {
     if (zero_.erase(x) && !cfg_.f32) return x + " = " + (sign == '-' ? "-(" + e + ")" : e) + ";";
     return x + (sign == '-' ? " -= " : " += ") + e + ";";
@@ -351,7 +354,7 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     // Loop exps the reverse sweep recomputes record wide arguments in the
     // forward sweep; the recompute itself takes the series when none was.
     if (recompute) exp_fn_ = series_exp_ ? "NT_EXP64_SERIES(" : "NT_EXP64(";
-    else if (lp_.recompute[j] && lp_.tape_slot[j] < 0) exp_fn_ = "NT_EXP64W(";
+    else if (lp_.recompute[j] && lp_.tape_slot[j] < 0) exp_fn_ = fwd_fast_ ? "NT_EXP64F(" : "NT_EXP64W(";
     if (bn.op == NT_CONST && bn.cslot >= 0)
       o_.line(name(j) + " = NT_CTAB(" + unit + ", " + std::to_string(bn.cslot) + ");");
     else
@@ -586,20 +589,42 @@ void Emitter::emit_scenario() {
       o_.close();
       o_.close();
     };
+    // Exps the reverse sweep recomputes run in the forward loop as the bare
+    // series, recording wide arguments; a warp that recorded one runs the
+    // loop again from its initial carries with the guarded routine (which
+    // rewrites the tape and the checkpoints).  GBM steps never take the redo.
+    bool fast_exp = false;
+    if (cfg_.target == 0 && (!cfg_.f32 || cfg_.wide32))
+      for (int32_t j = 0; j < L; ++j)
+        fast_exp |= lp_.body[j].op == NT_EXP && lp_.recompute[j] && lp_.tape_slot[j] < 0;
+    auto guarded_loop = [&]() {
+      if (!fast_exp) {
+        forward_loop();
+        return;
+      }
+      fwd_fast_ = true;
+      forward_loop();
+      fwd_fast_ = false;
+      o_.open("if (__any_sync(nt_lanes, nt_wide)) {  // an exp argument left the series range: redo guarded");
+      for (size_t c = 0; c < lp_.carries.size(); ++c)
+        o_.line("cv" + std::to_string(lp_.carries[c]) + " = " + val_outside(lp_.carry_init[c]) + ";");
+      forward_loop();
+      o_.close();
+    };
     bool taped_draws = false;
     for (int32_t j = 0; j < L; ++j) taped_draws |= is_draw(lp_.body[j].op) && lp_.tape_slot[j] >= 0;
     if (cfg_.markets && taped_draws) {
       // The first market draws and tapes them; the others read them back.
       o_.open("if (nt_m == 0) {");
-      forward_loop();
+      guarded_loop();
       o_.close("} else {");
       ++o_.ind;
       reuse_draws_ = true;
-      forward_loop();
+      guarded_loop();
       reuse_draws_ = false;
       o_.close();
     } else {
-      forward_loop();
+      guarded_loop();
     }
     emit_straight_forward(lp_.end(), t_.n);
   }

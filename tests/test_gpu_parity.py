@@ -222,6 +222,22 @@ def test_basket_config4_fp64(engine, oracle_mod):
     _assert_parity(got, want, scale)
 
 
+@pytest.mark.parametrize("vol,steps", [(0.476, 252), (2.0, 52)])
+def test_wide_exp_arguments_take_the_guarded_redo(engine, oracle_mod, vol, steps):
+    """GBM exps run in the forward loop as the bare series.  A warp in which
+    some lane's log-return leaves the series range (|x| > 1/8) reruns the
+    loop with the guarded exp, and its reverse sweep takes the guarded copy.
+    vol 0.476 over 252 steps puts a wide draw in about one path in 150 (some
+    warps redo, most do not); vol 2 over 52 steps makes every warp redo."""
+    tape = quant.asian_tape(steps)
+    x = [100.0, 100.0, vol, 0.03, 1.0]
+    with engine.compile(tape, FP64) as ex:
+        ex.setInputs(x)
+        got, _ = ex.replay_sums(40_000, 0x1_0000_0003, 42)
+    want, scale = _oracle(oracle_mod, tape, x, 40_000, 0x1_0000_0003, 42)
+    _assert_parity(got, want, scale)
+
+
 def test_cva_config5_fp64(engine, oracle_mod):
     """CVA of 100 payer swaps under Hull-White, 120 monthly
     dates; adjoints w.r.t. the 40 pillar zero rates and the hazard rate.  The
