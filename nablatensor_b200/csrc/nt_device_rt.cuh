@@ -240,6 +240,40 @@ NT_FN double nt_exp_small(double x) {
   return fma(p, x, 1.0);
 }
 
+/* exp(x) over the whole double range, without a branch (Cody and Waite 1980):
+ * k = rint(x / ln2) by the rounding constant 1.5 * 2^52, r = x - k ln2 with
+ * ln2 in two parts (the high part has 42 significant bits, so k * hi is exact
+ * for |k| < 2^11), |r| <= ln2 / 2, exp(r) by its Taylor series to r^13
+ * (truncation < 2^-57), then scaled by 2^(k/2) * 2^(k - k/2), each factor a
+ * normal power of two, so the overflow threshold and gradual underflow round
+ * once.  x is clamped to [-746, 710] first (exp is 0 or infinite beyond);
+ * NaN passes through. */
+NT_FN double nt_exp_cw(double x) {
+  const double xc = fmin(fmax(x, -746.0), 710.0);
+  const double kt = fma(xc, 0x1.71547652b82fep+0 /* 1/ln2 */, 0x1.8p52);
+  const double kd = kt - 0x1.8p52;
+  const int k = (int)nt_loword(kt);
+  double r = fma(kd, -0x1.62e42fefa3800p-1 /* ln2 hi */, xc);
+  r = fma(kd, -0x1.ef35793c76730p-45 /* ln2 lo */, r);
+  double p = 1.0 / 6227020800.0;       /* 1/13! */
+  p = fma(p, r, 1.0 / 479001600.0);    /* 1/12! */
+  p = fma(p, r, 1.0 / 39916800.0);     /* 1/11! */
+  p = fma(p, r, 1.0 / 3628800.0);      /* 1/10! */
+  p = fma(p, r, 1.0 / 362880.0);
+  p = fma(p, r, 1.0 / 40320.0);
+  p = fma(p, r, 1.0 / 5040.0);
+  p = fma(p, r, 1.0 / 720.0);
+  p = fma(p, r, 1.0 / 120.0);
+  p = fma(p, r, 1.0 / 24.0);
+  p = fma(p, r, 1.0 / 6.0);
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  const int k1 = k >> 1, k2 = k - k1;
+  const double y = (p * nt_from_words((k1 + 1023) << 20, 0u)) * nt_from_words((k2 + 1023) << 20, 0u);
+  return x != x ? x : y;
+}
+
 NT_FN double nt_exp64(double x) {
 #ifdef NT_HOST
   if (fabs(x) <= 0.125) return nt_exp_small(x);
@@ -276,41 +310,20 @@ NT_FN double nt_sqrt_pos(double a) {
 }
 
 #ifndef NT_HOST
-/* nt_exp64 with the warp's active lanes taken once per scenario by the
- * caller (the replay kernel's scenario body has no divergent region around
- * its EXP nodes), which saves the mask query at every node. */
-NT_FN double nt_exp64m(double x, unsigned lanes) {
-  double r = nt_exp_small(x);
-  const bool big = !(fabs(x) <= 0.125);
-  if (__any_sync(lanes, big)) {
-    if (big) r = exp(x);
-  }
-  return r;
-}
-#endif
-
-#ifndef NT_HOST
-/* nt_exp64m that also records in `wide` whether this lane's argument left the
- * series range.  A scenario whose forward sweep never did (for any lane of the
- * warp) recomputes its exps in the reverse sweep with the bare series: the
- * recomputed arguments are the forward's, so the result is the same, and the
- * segment's exps, free of branches, interleave. */
-NT_FN double nt_exp64w(double x, unsigned lanes, bool& wide) {
-  double r = nt_exp_small(x);
-  const bool big = !(fabs(x) <= 0.125);
-  wide |= big;
-  if (__any_sync(lanes, big)) {
-    if (big) r = exp(x);
-  }
-  return r;
+/* nt_exp_cw that also records in `wide` whether this lane's argument left the
+ * series range: the redo pass of the forward loop (see NT_EXP64F), after
+ * which the reverse sweep takes its guarded copy. */
+NT_FN double nt_exp_cw_flag(double x, bool& wide) {
+  wide |= !(fabs(x) <= 0.125);
+  return nt_exp_cw(x);
 }
 #endif
 
 #ifndef NT_HOST
 /* The forward loop's form of an exp the reverse sweep recomputes: the bare
  * series, with a wide argument recorded in `wide`.  A warp in which any lane
- * recorded one runs the loop again with nt_exp64w (the emitted kernel's redo
- * pass), so the series is only ever kept where it is accurate. */
+ * recorded one runs the loop again with nt_exp_cw_flag (the emitted kernel's
+ * redo pass), so the series is only ever kept where it is accurate. */
 NT_FN double nt_exp_series_flag(double x, bool& wide) {
   wide |= !(fabs(x) <= 0.125);
   return nt_exp_small(x);
@@ -320,18 +333,19 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
 /* EXP nodes of fp64 tapes: the dedicated routine on the device (the emitted
  * kernel declares nt_lanes = __activemask() and nt_wide at the top of each
  * scenario), libm in the host build (bit-for-bit with the oracle).
- * NT_EXP64F is the forward loop's form for an exp the reverse sweep recomputes
- * (the bare series, wide arguments recorded in nt_wide), NT_EXP64W the redo
- * pass's (guarded, recording too); NT_EXP64_SERIES is the recompute once the
- * forward sweep has shown every argument of the warp in the series range. */
+ * NT_EXP64 is the full-range routine (no branch); NT_EXP64F is the forward
+ * loop's form for an exp the reverse sweep recomputes (the bare series, wide
+ * arguments recorded in nt_wide), NT_EXP64W the redo pass's (full range,
+ * recording too); NT_EXP64_SERIES is the recompute once the forward sweep has
+ * shown every argument of the warp in the series range. */
 #ifdef NT_HOST
 #define NT_EXP64(x) exp(x)
 #define NT_EXP64W(x) exp(x)
 #define NT_EXP64F(x) exp(x)
 #define NT_EXP64_SERIES(x) exp(x)
 #else
-#define NT_EXP64(x) nt_exp64m((x), nt_lanes)
-#define NT_EXP64W(x) nt_exp64w((x), nt_lanes, nt_wide)
+#define NT_EXP64(x) nt_exp_cw(x)
+#define NT_EXP64W(x) nt_exp_cw_flag((x), nt_wide)
 #define NT_EXP64F(x) nt_exp_series_flag((x), nt_wide)
 #define NT_EXP64_SERIES(x) nt_exp_small(x)
 #endif

@@ -1,7 +1,8 @@
 """Accuracy of the dedicated fp64 routines in nt_device_rt.cuh.
 
 The device Box-Muller and the EXP fast path use routines written for the
-replay (nt_neg2log_u1, nt_sincos_2pi_u2, nt_exp_small).  Here they are
+replay (nt_neg2log_u1, nt_sincos_2pi_u2, nt_exp_small, the full-range
+nt_exp_cw).  Here they are
 compiled for the host from the same header and compared with x87 long-double
 libm (64-bit significand) over random generator words and the edge words
 (0, 1, 2^31, 2^32-1, the sqrt(2) fold, every quadrant boundary).  The bound
@@ -72,8 +73,33 @@ int main(void) {
     double ee = fabsl((long double)nt_exp_small(x) - we) / ulp_of((double)we);
     if (ee > worst_exp) worst_exp = ee;
   }
-  printf("%.6f %.6f %.6f %.6f %.6f %.6f %.6f\n", worst_log, worst_sin, worst_cos, worst_exp, worst_log_t,
-         worst_sin_t, worst_cos_t);
+  /* full-range exp: every binade of the argument from -745 to 709.78, the
+     thresholds, gradual underflow, and the special values */
+  double worst_cw = 0.0;
+  int special_ok = 1;
+  for (long i = 0; i < 3000000; ++i) {
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    const double u = (double)(st >> 11) * 0x1p-53;
+    double x;
+    if (i % 3 == 0) x = -745.0 + u * (709.78 + 745.0);            /* whole range */
+    else if (i % 3 == 1) x = (u - 0.5) * 2.0;                     /* near 0 */
+    else x = (u < 0.5 ? -1.0 : 1.0) * ldexp(1.0, -60 + (int)(u * 70.0)) * (1.0 + u);  /* tiny to ~1 */
+    const long double want = expl((long double)x);
+    const double got = nt_exp_cw(x);
+    const double w = (double)want;
+    double e;
+    if (w == 0.0) e = got == 0.0 ? 0.0 : 99.0;
+    else e = fabsl((long double)got - want) / ulp_of(w);
+    if (e > worst_cw) worst_cw = e;
+  }
+  const double specials[] = {0.0, -0.0, 709.78, 709.79, 710.0, 1e300, -744.4, -745.13, -745.2, -746.0, -1e300};
+  for (int i = 0; i < 11; ++i) {
+    const double x = specials[i], got = nt_exp_cw(x), want = exp(x);
+    if (!(got == want || fabs(got - want) <= ulp_of(want))) special_ok = 0;
+  }
+  if (!isinf(nt_exp_cw(INFINITY)) || nt_exp_cw(-INFINITY) != 0.0 || !isnan(nt_exp_cw(NAN))) special_ok = 0;
+  printf("%.6f %.6f %.6f %.6f %.6f %.6f %.6f %.6f %d\n", worst_log, worst_sin, worst_cos, worst_exp, worst_log_t,
+         worst_sin_t, worst_cos_t, worst_cw, special_ok);
   return 0;
 }
 """
@@ -89,7 +115,7 @@ def worst():
     subprocess.run(["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-I",
                     os.path.join(ROOT, "nablatensor_b200", "csrc"), "-o", exe, src, "-lm"], check=True)
     out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()
-    return dict(zip(["log", "sin", "cos", "exp", "log_t", "sin_t", "cos_t"], map(float, out)))
+    return dict(zip(["log", "sin", "cos", "exp", "log_t", "sin_t", "cos_t", "exp_cw", "special"], map(float, out)))
 
 
 def test_neg2log_u1_within_2_ulp(worst):
@@ -106,3 +132,11 @@ def test_sincos_within_2_ulp(worst):
 
 def test_exp_small_within_1_ulp(worst):
     assert worst["exp"] <= 1.0, worst
+
+
+def test_full_range_exp_within_1_ulp(worst):
+    """nt_exp_cw (the device's exp for arguments of any size) against
+    long-double exp over the whole range, with overflow, gradual underflow,
+    infinities and NaN."""
+    assert worst["exp_cw"] <= 1.0, worst
+    assert worst["special"] == 1.0, worst
