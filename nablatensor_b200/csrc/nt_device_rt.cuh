@@ -274,22 +274,6 @@ NT_FN double nt_exp_cw(double x) {
   return x != x ? x : y;
 }
 
-NT_FN double nt_exp64(double x) {
-#ifdef NT_HOST
-  if (fabs(x) <= 0.125) return nt_exp_small(x);
-  return exp(x);
-#else
-  // The series always; the library exp only when some lane of the warp needs
-  // it, so a warp of GBM steps never issues the general routine.
-  double r = nt_exp_small(x);
-  const bool big = !(fabs(x) <= 0.125);
-  if (__any_sync(__activemask(), big)) {
-    if (big) r = exp(x);
-  }
-  return r;
-#endif
-}
-
 /* sqrt of a positive normal argument (the Box-Muller radius): a reciprocal
  * square-root seed, two Newton steps, and one residual correction of the
  * root (Markstein's method); within 1 ulp. */

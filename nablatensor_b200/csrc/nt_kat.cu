@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(256) math_probe_kernel(int which, int iters, d
       case 2: acc += log(u); break;                                   // library log
       case 3: sincos(NT_TWO_PI * u, &s, &c); acc += s; acc2 += c; break;  // library sincos
       case 4: acc += sqrt(u * 46.0); break;                           // library sqrt
-      case 5: acc += nt_exp64((u - 0.5) * 0.25); break;               // dedicated exp
+      case 5: acc += nt_exp_cw((u - 0.5) * 0.25); break;              // full-range exp
       case 6: acc += nt_neg2log_u1(w); break;                         // dedicated -2 ln u1
       case 7: nt_sincos_2pi_u2(w, &s, &c); acc += s; acc2 += c; break;  // dedicated sincos
       case 8: acc += exp((u - 0.5) * 8.0); break;                     // library exp, wide range
