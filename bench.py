@@ -165,6 +165,62 @@ def cpu_baseline(wl: Workload, paths: int, threads: int = 0) -> dict:
                       f"{secs:.2f} s"}
 
 
+def cpu_compiled_baseline(wl: Workload, seconds: float = 5.0) -> dict:
+    """The analogue of the reference's `cpu-jit` engine: the emitter's host
+    C++ for the same tape (nt_emit_source target 1, straight-line within a
+    loop unit, every transcendental taped in the forward sweep as the
+    interpreter keeps its values), built with g++ -O3 -march=native and no FMA
+    contraction (the Java engines' semantics), run over contiguous path ranges
+    on every host thread.  A restatement, not the reference."""
+    from concurrent.futures import ThreadPoolExecutor
+    from nablatensor_b200 import _lib
+    tape = wl.tape()
+    x = np.ascontiguousarray(wl.inputs(tape), dtype=np.float64)
+    src = _lib.emit_source(tape, 1, precision=_lib.NT_FLOAT32 if wl.f32 else _lib.NT_FLOAT64,
+                           flags=_lib.NT_FLAG_TAPE_ALL)
+    d = tempfile.mkdtemp(prefix="nt_cpujit_")
+    cpp, so = os.path.join(d, "replay.cpp"), os.path.join(d, "replay.so")
+    with open(cpp, "w") as f:
+        f.write(src)
+    t0 = time.perf_counter()
+    subprocess.run(["g++", "-O3", "-march=native", "-std=c++17", "-ffp-contract=off", "-fno-fast-math", "-shared",
+                    "-fPIC", "-I", os.path.join(ROOT, "nablatensor_b200", "csrc"), "-o", so, cpp], check=True)
+    build_s = time.perf_counter() - t0
+    fn = ctypes.CDLL(so).nt_host_replay
+    fn.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
+                   ctypes.POINTER(ctypes.c_double)]
+    fn.restype = None
+    cores = os.cpu_count()
+    channels = tape.output_count() * (2 + tape.input_count())
+    xp = x.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+
+    def part(lo_n):
+        lo, n = lo_n
+        sums = np.zeros(channels, dtype=np.float64)
+        fn(xp, n, lo, wl.seed, sums.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+        return sums
+
+    def run(paths):
+        per = -(-paths // cores)
+        ranges = [(lo, min(per, paths - lo)) for lo in range(0, paths, per)]
+        with ThreadPoolExecutor(cores) as pool:
+            return sum(pool.map(part, ranges))
+
+    probe = 4 * cores
+    run(probe)  # warm (page-in, thread start)
+    t0 = time.perf_counter()
+    run(probe * 64)
+    rate = probe * 64 / (time.perf_counter() - t0)
+    paths = max(probe * 64, int(rate * seconds))
+    t0 = time.perf_counter()
+    run(paths)
+    secs = time.perf_counter() - t0
+    return {"value": paths / secs, "unit": "scenarios/s", "cores": cores, "kind": "restatement, not reference",
+            "sample": f"{paths} scenarios of the {wl.name} tape, {secs:.2f} s; the emitter's host C++ "
+                      f"(g++ -O3 -march=native, no FMA contraction, built in {build_s:.1f} s) on {cores} threads: "
+                      f"the analogue of the reference's cpu-jit engine"}
+
+
 def run_reference(args, rank: int, wl: Workload) -> None:
     if rank != 0:
         return
@@ -311,6 +367,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
                                    "burst (nt_fma_peak), the timed region being shorter than 1 s")),
                 "peak_burst": peak_burst, "peak_sustained": peak_sus, "frac_of_burst": achieved / peak_burst,
                 "flops_per_scenario": split[bound], "traffic": _profiled_traffic(wl, paths_per_launch)}
+    # arithmetic-only flops (transcendentals left out), against the fp64 pipe
+    roofline["arith_flops_per_scenario"] = info["arith_flops"]
+    roofline["arith_frac"] = info["arith_flops"] * paths_per_launch / kernel_s / 1e12 / peaks["fp64"][0]
     if wl.f32:
         roofline["flops_split"] = {k: {"flops_per_scenario": v, "frac": v * paths_per_launch / kernel_s / 1e12 /
                                        peaks[k][0]} for k, v in split.items()}
@@ -329,6 +388,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
                        "price": res.value(), "greeks": dict(zip(tape.input_names, map(float, res.gradients())))},
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "cpu_compiled": cpu_compiled_baseline(wl) if world == 1 and not args.no_cpu_compiled else None,
             "e2e": {"value": e2e_value, "unit": "scenarios/s", "h2d_bytes_per_step": 8 * len(x),
                     "d2h_bytes_per_step": 8 * info["channels"]},
             "gpu_launches": args.steps * launches_per_step,
@@ -386,6 +446,8 @@ def main():
     ap.add_argument("--paths", type=float, default=None, help="scenarios per step (default: the workload's)")
     ap.add_argument("--chunk", type=int, default=None, help="scenarios per launch (default: the workload's)")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000)
+    ap.add_argument("--no-cpu-compiled", action="store_true",
+                    help="skip the compiled-C++ CPU analogue (cpu_compiled)")
     ap.add_argument("--math-probes", action="store_true",
                     help="launch each math-probe kernel once (for ncu per-call instruction/flop counts)")
     args = ap.parse_args()

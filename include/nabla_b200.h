@@ -144,6 +144,8 @@ typedef struct nt_exec_info {
   double rev_flops;         /* algorithmic flops per scenario, reverse */
   double wide_flops;        /* fp32 tapes: the part of fwd_flops evaluated in fp64 (exp, log and
                                Box-Muller under the reference's fp32 semantics); 0 for fp64 tapes */
+  double arith_flops;       /* fwd_flops + rev_flops less the transcendentals (exp, log, sqrt and
+                               Box-Muller's log, sqrt, sincos): arithmetic-only flops per scenario */
 } nt_exec_info;
 
 /* ABI version (NT_ABI_VERSION of the built library). */

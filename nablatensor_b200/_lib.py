@@ -63,7 +63,7 @@ class NtExecInfo(ctypes.Structure):
         "ckpt_slots", "stored_per_unit", "ckpt_global", "tape_slots", "tape_mbytes", "markets_registers",
         "markets_local_bytes")] + [
         ("compile_seconds", ctypes.c_double), ("fwd_flops", ctypes.c_double), ("rev_flops", ctypes.c_double),
-        ("wide_flops", ctypes.c_double)]
+        ("wide_flops", ctypes.c_double), ("arith_flops", ctypes.c_double)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}

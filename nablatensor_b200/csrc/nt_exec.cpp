@@ -277,6 +277,7 @@ void Exec::load(int max_regs) {
   info.fwd_flops = plan.fwd_flops;
   info.rev_flops = plan.rev_flops;
   info.wide_flops = plan.wide_flops;
+  info.arith_flops = plan.arith_flops;
 }
 
 Exec::~Exec() {

@@ -102,6 +102,7 @@ struct Plan {
   double fwd_flops = 0.0;  // algorithmic, per scenario
   double rev_flops = 0.0;
   double wide_flops = 0.0;  // of fwd_flops: what an fp32 tape evaluates in fp64 (reference fp32 semantics)
+  double arith_flops = 0.0;  // fwd + rev without the transcendentals' weighted flops
   int32_t stored_per_unit = 0;
   int32_t per_unit_regs = 0;  // registers one loop unit's reverse values take (estimate)
 };

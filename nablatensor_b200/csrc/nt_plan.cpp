@@ -531,7 +531,7 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
   w.log = kFlopWeights[1];
   w.sqrt = kFlopWeights[2];
   w.sincos = kFlopWeights[3];
-  double fwd = 0, rev = 0, wide = 0;
+  double fwd = 0, rev = 0, wide = 0, transc = 0;
   for (int32_t i = 0; i < t.n; ++i) {
     const int op = t.op[i];
     // fp32 under the reference's semantics: exp, log and Box-Muller run in fp64.
@@ -547,13 +547,14 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
       case NT_NEG: fwd += w.neg; break;
       case NT_MAX: case NT_MIN: fwd += w.minmax; break;
       case NT_ABS: fwd += w.abs; break;
-      case NT_EXP: fwd += w.exp; break;
-      case NT_LOG: fwd += w.log; break;
-      case NT_SQRT: fwd += w.sqrt; break;
+      case NT_EXP: fwd += w.exp; transc += w.exp; break;
+      case NT_LOG: fwd += w.log; transc += w.log; break;
+      case NT_SQRT: fwd += w.sqrt; transc += w.sqrt; break;
       case NT_RANDN:
         // one Box-Muller pair per two normals: log + sqrt + sincos, plus
         // u1, u2 (2 adds, 2 multiplies), -2 ln u1, the angle, r*cos, r*sin = 8
         fwd += 0.5 * (w.log + w.sqrt + w.sincos + 8.0);
+        transc += 0.5 * (w.log + w.sqrt + w.sincos);
         break;
       case NT_RANDU: fwd += 2.0; break;
       default: break;
@@ -576,6 +577,7 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
   p.fwd_flops = fwd;
   p.wide_flops = wide;
   p.rev_flops = cfg.adjoints ? rev * t.n_out() : 0.0;
+  p.arith_flops = fwd - transc + p.rev_flops;
   return p;
 }
 

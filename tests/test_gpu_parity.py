@@ -146,6 +146,19 @@ def test_1m_against_oracle_exact(engine, oracle_mod):
     _assert_parity(got, want, scale)
 
 
+def test_flop_counts_of_the_asian_tape(engine):
+    """The roofline's flops per scenario for config 1: arithmetic 1,020 ops
+    forward, 4 per Box-Muller normal, 12 per step in the reverse sweep plus the
+    setup and tail; the weighted count adds 29 per exp, 13 per sqrt and
+    (44 + 13 + 36) per Box-Muller pair."""
+    with engine.compile(quant.asian_tape(252), FP64) as ex:
+        info = ex.info()
+    assert 5000 < info["arith_flops"] < 5200
+    weighted = 253 * 29.0 + 13.0 + 126 * (44.0 + 13.0 + 36.0)
+    assert info["fwd_flops"] + info["rev_flops"] - info["arith_flops"] == pytest.approx(weighted, abs=1e-9)
+    assert info["wide_flops"] == 0.0
+
+
 @pytest.mark.parametrize("seg_units", [1, 7, 21])
 def test_segment_lengths_agree(engine, seg_units):
     tape = quant.asian_tape(252)
