@@ -224,8 +224,10 @@ NT_FN void nt_sincos_2pi_u2(nt_u32 w1, double* sn, double* cs) {
   *cs = co;
 }
 
-/* exp(x): |x| <= 1/8 (every GBM log-return) by its Taylor series to x^10
- * (truncation < 2^-58 relative); otherwise the library exp. */
+/* exp(x) for |x| <= 1/8 (every GBM log-return) by its Taylor series to x^10
+ * (truncation < 2^-58 relative), in Horner form.  (Estrin's scheme, with a
+ * dependent chain of 6 instead of 11, measured slower in the replay: the
+ * kernel is bound by instructions issued, not by the chain.) */
 NT_FN double nt_exp_small(double x) {
   double p = 1.0 / 3628800.0;
   p = fma(p, x, 1.0 / 362880.0);
@@ -349,64 +351,93 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
 
 #ifdef NT_HOST
 #define NT_LN_TAB nt_ln_tab_g
+#define NT_LN_LO nt_ln_lo_g
 #define NT_SC_TAB nt_sc_tab_g
+#define NT_SC_ARG nt_sc_arg_g
 NT_FN void nt_math_tables_load(void) {}
 #else
-__shared__ double nt_ln_tab_s[NT_LN_TAB_N * 3];
-__shared__ double nt_sc_tab_s[NT_SC_TAB_N * 2];
+__shared__ __align__(16) double nt_ln_tab_s[NT_LN_TAB_N * 2];
+__shared__ double nt_ln_lo_s[NT_LN_TAB_N];
+__shared__ __align__(16) double nt_sc_tab_s[NT_SC_TAB_N * 2];
+__shared__ double nt_sc_arg_s[NT_SC_TAB_N];
 #define NT_LN_TAB nt_ln_tab_s
+#define NT_LN_LO nt_ln_lo_s
 #define NT_SC_TAB nt_sc_tab_s
+#define NT_SC_ARG nt_sc_arg_s
 /* Every thread of the block must call this before any Box-Muller draw. */
 NT_FN void nt_math_tables_load(void) {
-  for (int i = threadIdx.x; i < NT_LN_TAB_N * 3; i += blockDim.x) nt_ln_tab_s[i] = nt_ln_tab_g[i];
+  for (int i = threadIdx.x; i < NT_LN_TAB_N * 2; i += blockDim.x) nt_ln_tab_s[i] = nt_ln_tab_g[i];
+  for (int i = threadIdx.x; i < NT_LN_TAB_N; i += blockDim.x) nt_ln_lo_s[i] = nt_ln_lo_g[i];
   for (int i = threadIdx.x; i < NT_SC_TAB_N * 2; i += blockDim.x) nt_sc_tab_s[i] = nt_sc_tab_g[i];
+  for (int i = threadIdx.x; i < NT_SC_TAB_N; i += blockDim.x) nt_sc_arg_s[i] = nt_sc_arg_g[i];
   __syncthreads();
 }
 #endif
 
+/* Entry j of a two-wide table: one 16-byte load on the device. */
+NT_FN void nt_tab2(const double* tab, int j, double* a, double* b) {
+#ifdef NT_HOST
+  *a = tab[2 * j];
+  *b = tab[2 * j + 1];
+#else
+  const double2 p = reinterpret_cast<const double2*>(tab)[j];
+  *a = p.x;
+  *b = p.y;
+#endif
+}
+
 /* -2 ln(u1) by Tang's table method (ACM TOMS 15(2), 1989): u1 = m 2^k with m
  * folded into [0.75, 1.5); c_j = 0.75 + j/128 the nearest centre (c_32 = 1
- * exactly, so u1 near 1 keeps full relative precision); f = m - c_j exact;
- * t = f / c_j, |t| <= 1/192; ln(1 + t) to t^7 (truncation < 2^-60);
- * ln c_j tabulated as a double-double. */
+ * exactly, so u1 near 1 keeps full relative precision).  j and c_j come from
+ * the top 20 fraction bits of m in integer arithmetic: c_j is m rounded to 7
+ * fraction bits (6 when folded, where the binade is [0.5, 1)), a carry into
+ * the exponent giving c = 1 or 1.5 exactly; f = m - c_j is exact.  The table
+ * carries -2/c_j and -2 ln c_j (a double-double), so the factor -2 costs
+ * nothing: with v = -2 f / c_j, |v| <= 1/96,
+ * -2 ln(1 + f/c_j) = v + v^2/4 + v^3/12 + v^4/32 + v^5/80 + v^6/192 + v^7/448
+ * (the series of ln(1 + t) at t = -v/2; truncation below 2^-55 of the
+ * result), in Horner form. */
 NT_FN double nt_neg2log_u1_t(nt_u32 w0) {
-  const double u = ((double)w0 + 0.5) * NT_UINT_SCALE;
+  const double u = fma((double)w0, 0x1p-32, 0x1p-33); /* (w0 + 0.5) 2^-32, exact */
   const int hi = nt_hiword(u);
-  int k = ((hi >> 20) & 0x7ff) - 1023;
-  int mhi = (hi & 0x000fffff) | 0x3ff00000; /* m in [1, 2) */
-  if (mhi >= 0x3ff80000) {                   /* m >= 1.5: use m / 2 in [0.75, 1) */
-    mhi -= 0x00100000;
-    k += 1;
-  }
+  const int f20 = hi & 0x000fffff;
+  const bool fold = f20 >= 0x00080000; /* m >= 1.5: use m / 2 in [0.75, 1) */
+  const int k = (hi >> 20) - (fold ? 1022 : 1023);
+  const int mhi = f20 | (fold ? 0x3fe00000 : 0x3ff00000);
+  /* (m - 0.75) * 128 rounded: (f20 / 2^20 - 0.5) * 64 when folded, else 32 + f20 / 2^13 */
+  const int j = fold ? (f20 - 0x00080000 + 0x2000) >> 14 : 32 + ((f20 + 0x1000) >> 13);
+  const int chi = fold ? (mhi + 0x2000) & ~0x3fff : (mhi + 0x1000) & ~0x1fff;
   const double m = nt_from_words(mhi, nt_loword(u));
-  const int j = (int)((m - 0.75) * 128.0 + 0.5);
-  const double f = m - (0.75 + (double)j * 0.0078125); /* exact */
-  const double* e = &NT_LN_TAB[3 * j];
-  const double t = f * e[0];
-  double p = 1.0 / 7.0;
-  p = fma(p, t, -1.0 / 6.0);
-  p = fma(p, t, 1.0 / 5.0);
-  p = fma(p, t, -0.25);
-  p = fma(p, t, 1.0 / 3.0);
-  p = fma(p, t, -0.5);
-  const double l1p = fma(t * t, p, t);
+  double rc, lh;
+  nt_tab2(NT_LN_TAB, j, &rc, &lh);
+  const double v = (m - nt_from_words(chi, 0u)) * rc; /* m - c_j exact */
+  double p = 1.0 / 448.0;
+  p = fma(p, v, 1.0 / 192.0);
+  p = fma(p, v, 1.0 / 80.0);
+  p = fma(p, v, 1.0 / 32.0);
+  p = fma(p, v, 1.0 / 12.0);
+  p = fma(p, v, 0.25);
+  const double g = fma(v * v, p, v);
   const double kd = (double)k;
-  const double s1 = fma(kd, 0x1.62e42p-1 /* ln2 hi */, e[1]);
-  const double s2 = fma(kd, 0x1.fdf473de6af28p-22 /* ln2 lo */, e[2] + l1p);
-  return -2.0 * (s1 + s2);
+  const double s1 = fma(kd, -0x1.62e42p+0 /* -2 ln2 hi */, lh);
+  const double s2 = fma(kd, -0x1.fdf473de6af28p-21 /* -2 ln2 lo */, NT_LN_LO[j] + g);
+  return s1 + s2;
 }
 
 /* sin and cos of the reference's angle theta = fl(2 pi u2): theta = a_j + b
- * with a_j = j pi/128 tabulated, b in [0, pi/128) (pi/128 in two parts, j*hi
- * exact); sin b to b^7 and cos b - 1 to b^6 (truncation < 2^-61). */
+ * with j = w1 >> 24, the top 8 bits of the generator word, and a_j = j times
+ * pi/128 rounded to 33 significant bits, an exact double within 2.5e-10 of
+ * j pi/128; sin a_j and cos a_j are tabulated at that double, so b = theta -
+ * a_j (exact, Sterbenz) is the whole reduction.  Since u2 lies at least 2^-33
+ * inside [j/256, (j+1)/256), b is in (0, pi/128 + 2.5e-10) whatever theta's
+ * rounding; sin b to b^7 and cos b - 1 to b^6 (truncation < 2^-61). */
 NT_FN void nt_sincos_2pi_u2_t(nt_u32 w1, double* sn, double* cs) {
-  const double u2 = ((double)w1 + 0.5) * NT_UINT_SCALE;
+  const double u2 = fma((double)w1, 0x1p-32, 0x1p-33); /* (w1 + 0.5) 2^-32, exact */
   const double th = NT_TWO_PI * u2;
-  int j = (int)(th * NT_128_OVER_PI);
-  if (j > NT_SC_TAB_N - 1) j = NT_SC_TAB_N - 1;
-  const double jd = (double)j;
-  double b = fma(-jd, NT_PI_128_HI, th);
-  b = fma(-jd, NT_PI_128_LO, b);
+  const int j = (int)(w1 >> 24);
+  double S, C;
+  nt_tab2(NT_SC_TAB, j, &S, &C);
+  const double b = th - NT_SC_ARG[j];
   const double z = b * b;
   double ps = -1.0 / 5040.0;
   ps = fma(ps, z, 1.0 / 120.0);
@@ -416,7 +447,6 @@ NT_FN void nt_sincos_2pi_u2_t(nt_u32 w1, double* sn, double* cs) {
   pc = fma(pc, z, 1.0 / 24.0);
   pc = fma(pc, z, -0.5);
   const double cm1 = z * pc;
-  const double S = NT_SC_TAB[2 * j], C = NT_SC_TAB[2 * j + 1];
   *sn = S + fma(C, sb, S * cm1);
   *cs = C + fma(C, cm1, -S * sb);
 }

@@ -37,7 +37,8 @@ int main(void) {
   double worst_log_t = 0, worst_sin_t = 0, worst_cos_t = 0;
   const uint32_t edges[] = {0u, 1u, 2u, 0x7fffffffu, 0x80000000u, 0xffffffffu, 0xfffffffeu, 0x3fffffffu,
                             0x40000000u, 0xbfffffffu, 0xc0000000u, 0x6a09e667u, 0xb504f333u, 0xb504f334u,
-                            0x20000000u, 0x60000000u, 0xa0000000u, 0xe0000000u};
+                            0x20000000u, 0x60000000u, 0xa0000000u, 0xe0000000u, 0x00ffffffu, 0x01000000u,
+                            0xfeffffffu, 0xff000000u, 0x7f7fffffu, 0x80800000u, 0x5fffffffu, 0x9fffffffu};
   const int n_edges = sizeof(edges) / sizeof(edges[0]);
   for (long i = 0; i < 4000000 + n_edges; ++i) {
     uint32_t w;
