@@ -95,6 +95,14 @@ class Emitter {
   std::string exp_fn_ = "NT_EXP64(";
   // Forward loop pass that evaluates the recomputed exps by the bare series.
   bool fwd_fast_ = false;
+  // Gathered arguments that depend on no draw are the same for every path of
+  // a launch: the CUDA kernel evaluates them once per block into shared
+  // memory (nt_gvs[k * N + unit]) instead of a per-thread array per scenario.
+  bool gv_shared_ = false;
+  std::string gv_ref(int32_t k, const std::string& unit) const {
+    if (gv_shared_) return "nt_gvs[" + std::to_string(k * lp_.N) + " + " + unit + "]";
+    return "nt_gv" + std::to_string(k) + "[" + unit + "]";
+  }
   std::string contrib(const std::string& x, char sign, const std::string& e) {
     if (zero_.erase(x) && !cfg_.f32) return x + " = " + (sign == '-' ? "-(" + e + ")" : e) + ";";
     return x + (sign == '-' ? " -= " : " += ") + e + ";";
@@ -141,6 +149,8 @@ class Emitter {
   void emit_body_forward(const std::string& pre, const std::string& unit, bool recompute, int g);
   void emit_body_reverse(int g);
   void emit_scenario();
+  bool gather_is_launch_invariant() const;
+  void emit_shared_gather();
   void emit_reverse_for_output(int o);
   void acc_line(int32_t k, const std::string& x);
 };
@@ -290,7 +300,7 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
       if (g == 0) return "cs" + std::to_string(r.idx);
       return "r" + std::to_string(g - 1) + "_" + std::to_string(r.idx);
     }
-    if (r.kind == REF_GATHER) return "nt_gv" + std::to_string(r.idx) + "[" + unit + "]";
+    if (r.kind == REF_GATHER) return gv_ref(r.idx, unit);
     return val_outside(r.idx);
   };
   // Pairing of normal draws inside the unit.
@@ -375,7 +385,7 @@ void Emitter::emit_body_reverse(int g) {
       if (g == 0) return "cs" + std::to_string(r.idx);
       return "r" + std::to_string(g - 1) + "_" + std::to_string(r.idx);
     }
-    if (r.kind == REF_GATHER) return "nt_gv" + std::to_string(r.idx) + "[" + unit + "]";
+    if (r.kind == REF_GATHER) return gv_ref(r.idx, unit);
     return val_outside(r.idx);
   };
   auto adj = [&](const Ref& r, bool* active) -> std::string {
@@ -522,6 +532,58 @@ void Emitter::acc_line(int32_t k, const std::string& x) {
   else o_.line("nt_two_sum(&nt_acc[" + K + "], &nt_cmp[" + K + "], " + x + ");");
 }
 
+// True when no gathered node depends on a draw: then every path of a launch
+// reads the same gathered values.
+bool Emitter::gather_is_launch_invariant() const {
+  if (!lp_.present || lp_.gather.empty()) return false;
+  std::vector<uint8_t> drawn(lp_.B, 0);
+  for (int32_t i = 0; i < lp_.B; ++i) {
+    const int op = t_.op[i];
+    if (is_draw(op)) drawn[i] = 1;
+    else if (is_unary(op) || is_binary(op))
+      drawn[i] = drawn[t_.a[i]] | (is_binary(op) ? drawn[t_.b[i]] : 0);
+  }
+  for (const auto& g : lp_.gather)
+    for (int32_t x : g)
+      if (drawn[x]) return false;
+  return true;
+}
+
+// The gathered values' cone of prologue nodes, evaluated by every thread
+// before the path loop (no draw among them), written to shared memory by
+// thread 0.
+void Emitter::emit_shared_gather() {
+  std::vector<uint8_t> need(lp_.B, 0);
+  for (const auto& g : lp_.gather)
+    for (int32_t x : g) need[x] = 1;
+  for (int32_t i = lp_.B - 1; i >= 0; --i) {
+    if (!need[i]) continue;
+    const int op = t_.op[i];
+    if (is_unary(op) || is_binary(op)) need[t_.a[i]] = 1;
+    if (is_binary(op)) need[t_.b[i]] = 1;
+  }
+  const int32_t NG = (int32_t)lp_.gather.size();
+  o_.line("__shared__ real nt_gvs[" + std::to_string(NG * lp_.N) + "];");
+  o_.open("{  // gathered arguments: the same for every path of the launch");
+  const std::string saved = exp_fn_;
+  exp_fn_ = "NT_EXP64(";
+  for (int32_t i = 0; i < lp_.B; ++i) {
+    if (!need[i]) continue;
+    const int op = t_.op[i];
+    const std::string A = nargs(op) >= 1 ? val_outside(t_.a[i]) : "";
+    const std::string B = nargs(op) >= 2 ? val_outside(t_.b[i]) : "";
+    o_.line("const real v" + std::to_string(i) + " = " + fwd_expr(op, A, B, t_.c[i], t_.a[i]) + ";");
+  }
+  exp_fn_ = saved;
+  o_.open("if (threadIdx.x == 0) {");
+  for (int32_t k = 0; k < NG; ++k)
+    for (int32_t u = 0; u < lp_.N; ++u)
+      o_.line("nt_gvs[" + std::to_string(k * lp_.N + u) + "] = " + val_outside(lp_.gather[k][u]) + ";");
+  o_.close();
+  o_.close();
+  o_.line("__syncthreads();");
+}
+
 void Emitter::emit_scenario() {
   if (cfg_.target == 0) o_.line("bool nt_wide = false;  // some EXP argument left the series range");
   // Stream keys.
@@ -537,8 +599,9 @@ void Emitter::emit_scenario() {
     const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
     emit_straight_forward(0, lp_.B);
     // Gathered arguments: the prologue node each unit reads, as one array
-    // indexed by the unit.
-    for (size_t k = 0; k < lp_.gather.size(); ++k) {
+    // indexed by the unit (in shared memory, filled before the path loop,
+    // when they depend on no draw).
+    for (size_t k = 0; k < lp_.gather.size() && !gv_shared_; ++k) {
       std::string init;
       for (int32_t x : lp_.gather[k]) init += (init.empty() ? "" : ", ") + val_outside(x);
       o_.line("const real nt_gv" + std::to_string(k) + "[" + std::to_string(lp_.N) + "] = {" + init + "};");
@@ -661,6 +724,7 @@ void Emitter::emit_scenario() {
 std::string Emitter::run() {
   const bool host = cfg_.target == 1;
   const bool mk = cfg_.markets;
+  gv_shared_ = cfg_.target == 0 && !mk && gather_is_launch_invariant();
   const int32_t nck_total = ckpt_values(p_);
   o_.line("// Generated by libnabla_b200 from a " + std::to_string(t_.n) + "-node tape.");
   if (host) {
@@ -806,6 +870,7 @@ std::string Emitter::run() {
     }
   }
   o_.line("nt_math_tables_load();");
+  if (gv_shared_) emit_shared_gather();
   o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
   o_.line("const nt_u64 path = p + path_offset;");
   o_.line("const unsigned nt_lanes = __activemask();");
