@@ -367,6 +367,24 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
                                    "burst (nt_fma_peak), the timed region being shorter than 1 s")),
                 "peak_burst": peak_burst, "peak_sustained": peak_sus, "frac_of_burst": achieved / peak_burst,
                 "flops_per_scenario": split[bound], "traffic": _profiled_traffic(wl, paths_per_launch)}
+    # The value tape and the global checkpoints, written once in the forward
+    # sweep and read once in the reverse: the algorithmic HBM bytes.  A kernel
+    # whose tape moves more than its pipe allows is HBM-bound; the larger of
+    # the two fractions names the bound.
+    real_b = 4 if wl.f32 else 8
+    tape_b = 2 * real_b * (info["tape_slots"] * info["loop_units"]
+                           + (info["ckpt_slots"] * info["segments"] if info["ckpt_global"] else 0))
+    hbm_peak, hbm_src = _hbm_peak()
+    hbm_achieved = tape_b * paths_per_launch / kernel_s / 1e9
+    hbm = {"bound": "hbm", "achieved": hbm_achieved, "peak": hbm_peak, "unit": "GB/s",
+           "frac": hbm_achieved / hbm_peak, "peak_source": hbm_src, "bytes_per_scenario": tape_b,
+           "traffic": roofline["traffic"]}
+    if hbm["frac"] > roofline["frac"]:
+        pipe_roof = roofline
+        roofline = dict(hbm)
+        roofline["pipe"] = {k: v for k, v in pipe_roof.items() if k != "traffic"}
+    else:
+        roofline["hbm"] = {k: v for k, v in hbm.items() if k not in ("bound", "traffic")}
     # arithmetic-only flops (transcendentals left out), against the fp64 pipe
     roofline["arith_flops_per_scenario"] = info["arith_flops"]
     roofline["arith_frac"] = info["arith_flops"] * paths_per_launch / kernel_s / 1e12 / peaks["fp64"][0]
@@ -401,6 +419,15 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
     ex.close()
     if line is not None:
         emit(line)
+
+
+def _hbm_peak():
+    """The measured HBM copy bandwidth of this pool's B200s (GB/s)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (copy bandwidth), of measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "6.65 TB/s, an earlier copy measurement on this pool, of fallback"
 
 
 def _profiled_traffic(wl: Workload, paths_per_launch: float):
