@@ -402,7 +402,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
             "config": {"workload": f"{wl.name}: {wl.desc}", "paths_per_step": total, "chunk_paths": chunk, "l2": "flushed between timed steps "
                        f"(256 MiB write); inputs are {8 * len(x)} bytes", "kernel": {k: info[k] for k in (
                            "registers", "local_bytes", "blocks_per_sm", "grid", "loop_units", "seg_units",
-                           "segments", "ckpt_slots", "stored_per_unit")},
+                           "segments", "ckpt_slots", "stored_per_unit")} | {"nvrtc": _nvrtc_version()},
                        "price": res.value(), "greeks": dict(zip(tape.input_names, map(float, res.gradients())))},
             "roofline": roofline,
             "cpu_baseline": cpu,
@@ -419,6 +419,18 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
     ex.close()
     if line is not None:
         emit(line)
+
+
+def _nvrtc_version() -> str:
+    """The NVRTC that compiled the replay kernels: the first libnvrtc.so.12 in
+    the process (torch's bundled copy once torch is imported, as here)."""
+    try:
+        nv = ctypes.CDLL("libnvrtc.so.12")
+        major, minor = ctypes.c_int(0), ctypes.c_int(0)
+        nv.nvrtcVersion(ctypes.byref(major), ctypes.byref(minor))
+        return f"{major.value}.{minor.value}"
+    except OSError:
+        return "unknown"
 
 
 def _hbm_peak():
