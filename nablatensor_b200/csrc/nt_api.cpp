@@ -154,6 +154,7 @@ int nt_emit_source(const nt_tape* tape, const nt_options* options, int32_t targe
   return guarded([&] {
     nt::EmitConfig cfg = nt::config_from(options, target);
     nt::Tape t = nt::ingest(tape);
+    nt::reduce_pow2_divisions(t, cfg.f32);
     nt::Plan p = nt::plan_tape(t, cfg);
     if (options->block == 0) cfg.block = nt::auto_block(p);
     copy_out(nt::emit(t, p, cfg), buf, cap, len);

@@ -160,6 +160,7 @@ Exec* Exec::create(const nt_tape* tape, const nt_options* opt) {
   std::unique_ptr<Exec> x(new Exec());
   x->cfg = config_from(opt, 0);
   x->tape = ingest(tape);
+  reduce_pow2_divisions(x->tape, x->cfg.f32);
   x->device = opt->device;
   x->use_disk_cache = (opt->flags & NT_FLAG_NO_DISK_CACHE) == 0;
   x->plan = plan_tape(x->tape, x->cfg);

@@ -45,6 +45,13 @@ struct Tape {
 // malformed index, op code or count.
 Tape ingest(const nt_tape* t);
 
+// Division by a constant power of two becomes multiplication by its exact
+// reciprocal (x / 2^k and x * 2^-k are the same correctly rounded number, and
+// so are the adjoint contributions d / 2^k and d * 2^-k), when the constant
+// node feeds nothing else and both 2^k and 2^-k are normal in the working
+// precision.  Returns the number of divisions rewritten.
+int32_t reduce_pow2_divisions(Tape& t, bool f32);
+
 // How a loop-body argument is reached.
 // An argument of a loop unit: the same unit, the previous unit (a carry), one
 // fixed node before the loop (an invariant), or a node before the loop that

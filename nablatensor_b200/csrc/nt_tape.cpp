@@ -3,6 +3,7 @@
 // The C ABI borrows the caller's flat arrays; ingest() copies them and checks
 // every index before anything is emitted, so a malformed tape becomes an
 // NT_E_TAPE status instead of an out-of-bounds access in generated code.
+#include <cmath>
 #include <sstream>
 
 #include "nt_internal.hpp"
@@ -94,6 +95,38 @@ Tape ingest(const nt_tape* src) {
     else t.active[i] = t.active[t.a[i]] || t.active[t.b[i]];
   }
   return t;
+}
+
+int32_t reduce_pow2_divisions(Tape& t, bool f32) {
+  std::vector<int32_t> uses(t.n, 0), div_uses(t.n, 0);
+  for (int32_t i = 0; i < t.n; ++i) {
+    const int op = t.op[i];
+    if (is_unary(op) || is_binary(op)) ++uses[t.a[i]];
+    if (is_binary(op)) ++uses[t.b[i]];
+    if (op == NT_DIV && t.a[i] != t.b[i]) ++div_uses[t.b[i]];
+  }
+  for (int32_t o : t.output_node) ++uses[o];  // an output constant keeps its value
+  const int max_exp = f32 ? 126 : 1022;
+  auto pow2 = [&](double c) {
+    if (!std::isfinite(c) || c == 0.0) return false;
+    int e = 0;
+    const double m = std::frexp(std::fabs(c), &e);  // |c| = m 2^e, m in [0.5, 1)
+    return m == 0.5 && std::abs(e - 1) <= max_exp;
+  };
+  int32_t n = 0;
+  for (int32_t i = 0; i < t.n; ++i) {
+    if (t.op[i] != NT_DIV) continue;
+    const int32_t b = t.b[i];
+    if (t.op[b] != NT_CONST || uses[b] != div_uses[b] || !pow2(t.c[b])) continue;
+    // every use of b is a division by it: the node can hold the reciprocal
+    for (int32_t k = i; k < t.n; ++k)
+      if (t.op[k] == NT_DIV && t.b[k] == b) {
+        t.op[k] = NT_MUL;
+        ++n;
+      }
+    t.c[b] = 1.0 / t.c[b];
+  }
+  return n;
 }
 
 }  // namespace nt

@@ -145,3 +145,20 @@ def term_vol_asian(steps=24):
         payoff = acc.div(float(steps)).sub(strike).max(0.0)
         rec.output(payoff.mul(rate.neg().exp()))
     return AadRecorder.record(body)
+
+
+def pow2_divisions(steps=24, tiny=2.0 ** -1000):
+    """Divisions by constants: powers of two (rewritten to a multiplication by
+    the exact reciprocal: 2, 0.5, 1, -4 and `tiny`), a power of two that also
+    feeds an addition (kept a division), and 3 (kept)."""
+    def body(rec):
+        s = rec.input("s", 1.5)
+        v = rec.input("v", 0.3)
+        shared = rec.constant(2.0)
+        acc = s
+        for _ in range(steps):
+            z = rec.randn()
+            x = acc.div(2.0).add(v.mul(z).div(0.5)).div(1.0).add(z.div(-4.0)).add(acc.div(3.0))
+            acc = x.div(shared).add(shared).mul(0.25).add(v.div(tiny).mul(tiny))
+        rec.output(acc)
+    return AadRecorder.record(body)

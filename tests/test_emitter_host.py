@@ -18,7 +18,7 @@ from oracle.oracle import FlatTape
 
 from conftest import host_kernel
 from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, nonuniform_asian,
-                   odd_steps_asian, random_branching, term_vol_asian)
+                   odd_steps_asian, pow2_divisions, random_branching, term_vol_asian)
 
 ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
 
@@ -175,3 +175,18 @@ def test_loop_plan_reported_for_config_tapes(ntlib):
     src = _lib.emit_source(quant.barrier_tape(252), target=0, precision=0)
     assert "step loop: 126 units of 32 nodes (2 steps each)" in src
     assert "nt_normal_pair32" in src
+
+
+@pytest.mark.parametrize("f32", [False, True])
+def test_power_of_two_divisions_become_exact_multiplications(oracle_mod, f32):
+    """Division by a constant power of two is emitted as multiplication by
+    the reciprocal, with bit-identical results (forward and adjoint); a
+    shared constant and a non-power of two stay divisions.  Per step the tape
+    has 7 divisions; 5 are by an unshared power of two (2, 0.5, 1, -4, tiny)."""
+    steps = 24
+    tape = pow2_divisions(steps, tiny=2.0 ** -100 if f32 else 2.0 ** -1000)
+    assert sum(1 for op in tape.op if op == 7) == 7 * steps
+    _run(oracle_mod, tape, [1.5, 0.3], 2_000, 7, 42, f32=f32)
+    src = _run(oracle_mod, tape, [1.5, 0.3], 500, 7, 42, f32=f32, flags=_lib.NT_FLAG_NO_LOOP)
+    # straight-line code: the 2 kept divisions per step, and their d/vb rules
+    assert sum(line.count(" / ") for line in src.splitlines()) == 4 * steps
