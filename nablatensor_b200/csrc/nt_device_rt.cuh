@@ -298,7 +298,7 @@ NT_FN double nt_sqrt_pos(double a) {
 #ifndef NT_HOST
 /* nt_exp_cw that also records in `wide` whether this lane's argument left the
  * series range: the redo pass of the forward loop (see NT_EXP64F), after
- * which the reverse sweep takes its guarded copy. */
+ * which the reverse sweep takes its full-range copy. */
 NT_FN double nt_exp_cw_flag(double x, bool& wide) {
   wide |= !(fabs(x) <= 0.125);
   return nt_exp_cw(x);

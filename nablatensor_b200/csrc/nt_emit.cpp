@@ -654,7 +654,7 @@ void Emitter::emit_scenario() {
     };
     // Exps the reverse sweep recomputes run in the forward loop as the bare
     // series, recording wide arguments; a warp that recorded one runs the
-    // loop again from its initial carries with the guarded routine (which
+    // loop again from its initial carries with the full-range routine (which
     // rewrites the tape and the checkpoints).  GBM steps never take the redo.
     bool fast_exp = false;
     if (cfg_.target == 0 && (!cfg_.f32 || cfg_.wide32))
@@ -668,7 +668,7 @@ void Emitter::emit_scenario() {
       fwd_fast_ = true;
       forward_loop();
       fwd_fast_ = false;
-      o_.open("if (__any_sync(nt_lanes, nt_wide)) {  // an exp argument left the series range: redo guarded");
+      o_.open("if (__any_sync(nt_lanes, nt_wide)) {  // an exp argument left the series range: redo, full range");
       for (size_t c = 0; c < lp_.carries.size(); ++c)
         o_.line("cv" + std::to_string(lp_.carries[c]) + " = " + val_outside(lp_.carry_init[c]) + ";");
       forward_loop();
@@ -701,7 +701,7 @@ void Emitter::emit_scenario() {
     // The reverse sweep recomputes EXP nodes when they are not taped
     // (draws-only tape, recompute-all).  On the device it is emitted twice:
     // the copy for warps whose forward exps all stayed in the series range
-    // uses the bare series, the other the guarded routine.
+    // uses the bare series, the other the full-range routine.
     bool rev_exp = false;
     if (lp_.present && cfg_.target == 0 && (!cfg_.f32 || cfg_.wide32))
       for (int32_t j = 0; j < lp_.L; ++j)
