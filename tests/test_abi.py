@@ -154,3 +154,26 @@ def test_recorded_tapes_round_trip_through_the_abi(ntlib):
     t = AadRecorder.record(lambda rec: rec.output(rec.input("x", 1.0).mul(2.0)))
     src = _lib.emit_source(t, target=1)
     assert "nt_host_replay" in src
+
+
+def _header_fields(struct: str):
+    with open(os.path.join(ROOT, "include", "nabla_b200.h")) as f:
+        text = f.read()
+    body = re.search(r"typedef struct " + struct + r" \{(.*?)\} " + struct + ";", text, re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    return [re.search(r"(\w+)\s*;", line).group(1) for line in body.split("\n") if ";" in line]
+
+
+@pytest.mark.parametrize("struct,cls", [("nt_tape", _lib.NtTape), ("nt_options", _lib.NtOptions),
+                                        ("nt_exec_info", _lib.NtExecInfo)])
+def test_ctypes_layouts_follow_the_header(struct, cls):
+    assert [name for name, _ in cls._fields_] == _header_fields(struct)
+
+
+def test_java_options_layout_follows_the_header():
+    """The FFM StructLayout shown to integrators names every nt_options field
+    in order (a missing trailing field would be read from past the end)."""
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+        text = f.read()
+    layout = re.search(r"StructLayout OPTIONS = MemoryLayout\.structLayout\((.*?)\);", text, re.S).group(1)
+    assert re.findall(r'withName\("(\w+)"\)', layout) == _header_fields("nt_options")
