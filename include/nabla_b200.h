@@ -108,7 +108,8 @@ typedef struct nt_options {
   int32_t min_blocks;  /* __launch_bounds__ minimum blocks per SM */
   int32_t max_regs;    /* register cap per thread */
   int32_t flags;       /* NT_FLAG_* */
-  int32_t fwd_unroll;  /* unroll of the forward step-unit loop */
+  int32_t fwd_unroll;  /* unroll of the forward step-unit loop; 0: the whole checkpoint segment, so
+                          one unit's draws and transcendentals overlap the previous unit's chain */
   int32_t grid_blocks_per_sm; /* cap on resident blocks per SM of the persistent grid */
 } nt_options;
 

@@ -631,12 +631,15 @@ void Emitter::emit_scenario() {
         o_.line("if (s + 1 < " + std::to_string(K) + " && threadIdx.x == 0) nt_prefetch_l2_bulk(nt_tape_blk + "
                 "(nt_u64)(s + 1) * (" + seg + "), (unsigned)(" + seg + " * sizeof(real)));");
       }
-      // A market that reads its draws back unrolls the segment, so the
-      // segment's tape loads are all in flight before the first unit needs
-      // one; the drawing loop stays rolled (it only stores).
+      // The segment's units are unrolled by default: a unit's draws and
+      // transcendentals depend only on its counter, so the compiler overlaps
+      // them with the previous unit's carry chain (+13 % on the 252-step
+      // Asian).  A market that reads its draws back unrolls the segment too,
+      // so the segment's tape loads are all in flight before the first unit
+      // needs one.
       if (cfg_.target == 0)
-        o_.line(reuse_draws_ ? std::string("#pragma unroll")
-                             : "#pragma unroll " + std::to_string(std::max(1, cfg_.fwd_unroll)));
+        o_.line(reuse_draws_ || cfg_.fwd_unroll <= 0 ? std::string("#pragma unroll")
+                                                      : "#pragma unroll " + std::to_string(cfg_.fwd_unroll));
       o_.open("for (int g = 0; g < " + std::to_string(G) + "; ++g) {");
       o_.line("const int u = s * " + std::to_string(G) + " + g;");
       std::string decl;

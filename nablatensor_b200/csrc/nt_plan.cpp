@@ -343,7 +343,7 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   cfg.seg_units = opt->seg_units;
   cfg.target = target;
   if (opt->fwd_unroll < 0 || opt->fwd_unroll > 16) fail(NT_E_INVALID_ARG, "fwd_unroll must be in [0, 16]");
-  cfg.fwd_unroll = opt->fwd_unroll > 0 ? opt->fwd_unroll : 1;
+  cfg.fwd_unroll = opt->fwd_unroll;
   cfg.acc_smem = (opt->flags & NT_FLAG_ACC_REGS) == 0;
   cfg.tape = (opt->flags & NT_FLAG_RECOMPUTE_ALL) == 0;
   cfg.tape_all = (opt->flags & NT_FLAG_TAPE_DRAWS) == 0;
