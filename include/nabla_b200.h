@@ -111,6 +111,7 @@ typedef struct nt_options {
   int32_t fwd_unroll;  /* unroll of the forward step-unit loop; 0: the whole checkpoint segment, so
                           one unit's draws and transcendentals overlap the previous unit's chain */
   int32_t grid_blocks_per_sm; /* cap on resident blocks per SM of the persistent grid */
+  int32_t rev_unroll;  /* unroll of the reverse sweep's segment loop (0 or 1: rolled) */
 } nt_options;
 
 typedef struct nt_exec nt_exec;

@@ -53,7 +53,7 @@ class NtOptions(ctypes.Structure):
     _fields_ = [("precision", ctypes.c_int32), ("adjoints", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("block", ctypes.c_int32), ("seg_units", ctypes.c_int32), ("min_blocks", ctypes.c_int32),
                 ("max_regs", ctypes.c_int32), ("flags", ctypes.c_int32), ("fwd_unroll", ctypes.c_int32),
-                ("grid_blocks_per_sm", ctypes.c_int32)]
+                ("grid_blocks_per_sm", ctypes.c_int32), ("rev_unroll", ctypes.c_int32)]
 
 
 class NtExecInfo(ctypes.Structure):
@@ -189,9 +189,9 @@ def tape_struct(tape):
 
 
 def options_struct(precision=NT_FLOAT64, adjoints=True, device=0, block=0, seg_units=0, min_blocks=0, max_regs=0,
-                   flags=0, fwd_unroll=0, grid_blocks_per_sm=0) -> NtOptions:
+                   flags=0, fwd_unroll=0, grid_blocks_per_sm=0, rev_unroll=0) -> NtOptions:
     return NtOptions(int(precision), int(bool(adjoints)), int(device), int(block), int(seg_units), int(min_blocks),
-                     int(max_regs), int(flags), int(fwd_unroll), int(grid_blocks_per_sm))
+                     int(max_regs), int(flags), int(fwd_unroll), int(grid_blocks_per_sm), int(rev_unroll))
 
 
 def emit_source(tape, target: int = 0, **opts) -> str:

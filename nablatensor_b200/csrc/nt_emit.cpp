@@ -469,6 +469,7 @@ void Emitter::emit_reverse_for_output(int o) {
     for (size_t k = 0; k < lp_.gather.size(); ++k)
       if (gather_active((int32_t)k))
         o_.line("real nt_gd" + std::to_string(k) + "[" + std::to_string(lp_.N) + "] = {};");
+    if (cfg_.target != 1 && cfg_.rev_unroll > 1) o_.line("#pragma unroll " + std::to_string(cfg_.rev_unroll));
     o_.open("for (int s = " + std::to_string(K - 1) + "; s >= 0; --s) {");
     for (int32_t c = 0; c < nck; ++c)
       o_.line("const real cs" + std::to_string(lp_.ckpt[c]) + " = NT_CK(s * " + std::to_string(nck) + " + " +

@@ -175,6 +175,7 @@ Exec* Exec::create(const nt_tape* tape, const nt_options* opt) {
   x->inputs.assign(x->tape.n_in(), 0.0);
   for (int32_t j = 0; j < x->tape.n_in(); ++j) x->inputs[j] = tape->constant[x->tape.input_node[j]];
   x->auto_regs = opt->max_regs == 0 && opt->min_blocks == 0;
+  x->auto_seg = x->auto_regs && opt->seg_units == 0 && opt->block == 0;
   x->load(opt->max_regs);
   return x.release();
 }
@@ -223,6 +224,42 @@ void Exec::load(int max_regs) {
     cu_check(d.funcGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, function), "cuFuncGetAttribute");
   }
   cu_check(d.funcGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, function), "cuFuncGetAttribute");
+  if (auto_seg && cfg.global_ckpt && plan.loop.present && plan.loop.G == 1 && plan.loop.K >= 4 && regs <= 192 &&
+      local == 0) {
+    // A heavy unit (one unit per segment) whose kernel left registers
+    // unused: two units per segment give the reverse sweep two units of
+    // independent work to overlap (the 10-asset basket: +17 %).  Kept when
+    // the wider kernel still fits in 255 registers without spilling; the
+    // choice depends only on the compiler's register count, never on timing.
+    EmitConfig c2 = cfg;
+    c2.seg_units = 2;
+    Plan p2 = plan_tape(tape, c2);
+    if (p2.loop.present && p2.loop.G == 2) {
+      c2.seg_units = cfg.seg_units;
+      std::string s2 = emit(tape, p2, c2);
+      double secs2 = 0.0;
+      std::vector<char> bin2 = nvrtc_compile(s2, "sm_100a", use_disk_cache, &secs2, cfg.fmad, max_regs);
+      secs += secs2;
+      CUmodule m2 = nullptr;
+      CUfunction f2 = nullptr;
+      cu_check(d.moduleLoadData(&m2, bin2.data()), "cuModuleLoadData");
+      cu_check(d.moduleGetFunction(&f2, m2, "nt_replay_kernel"), "cuModuleGetFunction");
+      int regs2 = 0, local2 = 0;
+      cu_check(d.funcGetAttribute(&regs2, CU_FUNC_ATTRIBUTE_NUM_REGS, f2), "cuFuncGetAttribute");
+      cu_check(d.funcGetAttribute(&local2, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f2), "cuFuncGetAttribute");
+      if (regs2 < 255 && local2 == 0) {
+        cu_check(d.moduleUnload(module), "cuModuleUnload");
+        module = m2;
+        function = f2;
+        plan = std::move(p2);
+        source = std::move(s2);
+        regs = regs2;
+        local = local2;
+      } else {
+        cu_check(d.moduleUnload(m2), "cuModuleUnload");
+      }
+    }
+  }
   cu_check(d.funcGetAttribute(&ssm, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, function), "cuFuncGetAttribute");
   int per_sm = 0;
   cu_check(d.occupancy(&per_sm, function, cfg.block, (size_t)dyn_smem), "cuOccupancyMaxActiveBlocksPerMultiprocessor");

@@ -26,6 +26,7 @@ struct Exec {
   int device = -1;
   bool use_disk_cache = true;
   int max_regs_opt = 0;  // nt_options.max_regs, kept for the kernels compiled later
+  bool auto_seg = true;   // no segment length or block size given: load() may widen a one-unit segment
   bool auto_regs = true;  // no register cap or block minimum given: load() may cap a kernel that ran out
   CUmodule module = nullptr;
   CUfunction function = nullptr;

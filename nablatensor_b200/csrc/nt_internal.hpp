@@ -127,6 +127,7 @@ struct EmitConfig {
   bool tape_every_exp = false;  // tape_all: also the exps of draws and invariants alone
   int32_t grid_blocks_per_sm = 0;  // 0: as many as fit
   int32_t fwd_unroll = 0;  // unroll of the forward unit loop, 0: the whole segment
+  int32_t rev_unroll = 1;  // unroll of the reverse segment loop
   int32_t block = 128;
   int32_t min_blocks = 0;
   int32_t max_regs = 0;    // register cap (__maxnreg__; launch bounds would override --maxrregcount)

@@ -344,6 +344,8 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   cfg.target = target;
   if (opt->fwd_unroll < 0 || opt->fwd_unroll > 16) fail(NT_E_INVALID_ARG, "fwd_unroll must be in [0, 16]");
   cfg.fwd_unroll = opt->fwd_unroll;
+  if (opt->rev_unroll < 0 || opt->rev_unroll > 8) fail(NT_E_INVALID_ARG, "rev_unroll must be in [0, 8]");
+  cfg.rev_unroll = std::max(1, opt->rev_unroll);
   cfg.acc_smem = (opt->flags & NT_FLAG_ACC_REGS) == 0;
   cfg.tape = (opt->flags & NT_FLAG_RECOMPUTE_ALL) == 0;
   cfg.tape_all = (opt->flags & NT_FLAG_TAPE_DRAWS) == 0;

@@ -164,7 +164,7 @@ class AadExecutable:
 
 
 _ENGINE_KEYS = {"block": "block", "segUnits": "seg_units", "minBlocks": "min_blocks", "maxRegs": "max_regs",
-                "fwdUnroll": "fwd_unroll", "gridBlocksPerSm": "grid_blocks_per_sm"}
+                "fwdUnroll": "fwd_unroll", "gridBlocksPerSm": "grid_blocks_per_sm", "revUnroll": "rev_unroll"}
 _ENGINE_FLAGS = {"noLoop": _lib.NT_FLAG_NO_LOOP, "sharedCheckpoints": _lib.NT_FLAG_SHARED_CKPT,
                  "fp32Fast": _lib.NT_FLAG_F32_FAST, "noFmad": _lib.NT_FLAG_NO_FMAD,
                  "accRegisters": _lib.NT_FLAG_ACC_REGS, "recomputeAll": _lib.NT_FLAG_RECOMPUTE_ALL,

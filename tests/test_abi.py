@@ -99,6 +99,10 @@ def test_invalid_arguments(ntlib):
         with pytest.raises(_lib.NablaError) as e:
             _lib.emit_source(quant.asian_tape(4), max_regs=regs)
         assert e.value.code == _lib.NT_E_INVALID_ARG and "max_regs" in str(e.value)
+    for key, bad in (("fwd_unroll", 17), ("fwd_unroll", -1), ("rev_unroll", 9), ("rev_unroll", -1)):
+        with pytest.raises(_lib.NablaError) as e:
+            _lib.emit_source(quant.asian_tape(4), **{key: bad})
+        assert e.value.code == _lib.NT_E_INVALID_ARG and key in str(e.value)
 
 
 def test_bad_block_size_is_an_argument_error(ntlib):

@@ -228,11 +228,17 @@ def test_basket_config4_fp64(engine, oracle_mod):
     """10-asset basket, 52 weekly steps, 21 Greeks."""
     tape = quant.basket_tape()
     assert tape.input_count() == 21
-    with engine.compile(tape, FP64) as ex:
-        assert ex.info()["loop_units"] == 52
+    one = FP64.with_engine_option("cuda", "segUnits", "1")
+    with engine.compile(tape, FP64) as ex, engine.compile(tape, one) as ex1:
+        # automatic: one unit per segment, widened to two when the kernel
+        # has the registers; an explicit segment length is kept as given
+        assert ex.info()["loop_units"] == 52 and ex.info()["seg_units"] in (1, 2)
+        assert ex1.info()["seg_units"] == 1
         got, _ = ex.replay_sums(20_000, 0x1_0000_0003, 7)
+        got1, _ = ex1.replay_sums(20_000, 0x1_0000_0003, 7)
     want, scale = _oracle(oracle_mod, tape, tape.recordedInputs(), 20_000, 0x1_0000_0003, 7)
     _assert_parity(got, want, scale)
+    _assert_parity(got1, want, scale)
 
 
 @pytest.mark.parametrize("vol,steps", [(0.476, 252), (2.0, 52)])
