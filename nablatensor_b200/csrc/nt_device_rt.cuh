@@ -224,22 +224,32 @@ NT_FN void nt_sincos_2pi_u2(nt_u32 w1, double* sn, double* cs) {
   *cs = co;
 }
 
-/* exp(x) for |x| <= 1/8 (every GBM log-return) by its Taylor series to x^10
- * (truncation < 2^-58 relative), in Horner form.  (Estrin's scheme, with a
- * dependent chain of 6 instead of 11, measured slower in the replay: the
- * kernel is bound by instructions issued, not by the chain.) */
+/* The generated tables and constants (nt_math_tables.cuh, 60-digit decimal
+ * arithmetic): the Box-Muller tables below and the exp series coefficients. */
+#ifdef NT_HOST
+#define NT_TABLE_QUAL const
+#else
+#define NT_TABLE_QUAL __device__ const
+#endif
+#include "nt_math_tables.cuh"
+
+/* exp(x) for |x| <= 1/8 (every GBM log-return): 1 + x (1 + x q(x)) with q
+ * the degree-7 polynomial interpolating (e^x - 1 - x) / x^2 at the 8
+ * Chebyshev nodes of [-1/8, 1/8] (coefficients in nt_math_tables.cuh; 2.2e-18
+ * relative error with the rounded coefficients), in Horner form: 9 FMAs, one
+ * fewer than the Taylor series to x^10 of the same accuracy.  (Estrin's
+ * scheme measured slower in the replay: the kernel is bound by the fp64 pipe
+ * and by instructions issued, not by the dependent chain.) */
 NT_FN double nt_exp_small(double x) {
-  double p = 1.0 / 3628800.0;
-  p = fma(p, x, 1.0 / 362880.0);
-  p = fma(p, x, 1.0 / 40320.0);
-  p = fma(p, x, 1.0 / 5040.0);
-  p = fma(p, x, 1.0 / 720.0);
-  p = fma(p, x, 1.0 / 120.0);
-  p = fma(p, x, 1.0 / 24.0);
-  p = fma(p, x, 1.0 / 6.0);
-  p = fma(p, x, 0.5);
-  p = fma(p, x, 1.0);
-  return fma(p, x, 1.0);
+  double q = NT_EXPS_C7;
+  q = fma(q, x, NT_EXPS_C6);
+  q = fma(q, x, NT_EXPS_C5);
+  q = fma(q, x, NT_EXPS_C4);
+  q = fma(q, x, NT_EXPS_C3);
+  q = fma(q, x, NT_EXPS_C2);
+  q = fma(q, x, NT_EXPS_C1);
+  q = fma(q, x, NT_EXPS_C0);
+  return fma(fma(q, x, 1.0), x, 1.0);
 }
 
 /* exp(x) over the whole double range, without a branch (Cody and Waite 1980):
@@ -342,12 +352,6 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
  * shorter dependent chains than the series above.  On the device every block
  * stages the tables in shared memory (nt_math_tables_load) before its first
  * draw; the host build reads the constant arrays. */
-#ifdef NT_HOST
-#define NT_TABLE_QUAL const
-#else
-#define NT_TABLE_QUAL __device__ const
-#endif
-#include "nt_math_tables.cuh"
 
 #ifdef NT_HOST
 #define NT_LN_TAB nt_ln_tab_g
