@@ -353,6 +353,22 @@ int nt_fma_peak_sustained(int32_t device, int32_t fp64, int32_t millis, double* 
  * exp, 13 one Philox2x32-10 block.  No counterpart in the reference. */
 int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 
+/* Evaluates one of the replay's dedicated fp64 routines on the device over n
+ * host inputs (copied in and out), so the tests can measure their accuracy as
+ * compiled for sm_100a:
+ *   which 0: out0[i] = -2 ln(u1), u1 = (words[i] + 0.5) 2^-32 (table-driven)
+ *   which 1: out0[i], out1[i] = sin, cos of fl(2 pi u2), u2 from words[i]
+ *   which 2: out0[i] = the Box-Muller radius sqrt of x[i] (x[i] > 0, normal)
+ *   which 3: out0[i] = the series exp of x[i] (|x[i]| <= 1/8)
+ *   which 4: out0[i] = the full-range exp of x[i]
+ *   which 5: out0[i], out1[i] = the cosine and sine Box-Muller legs of the
+ *            word pair (words[2i], words[2i+1])
+ * words is read for which 0, 1 (n words) and 5 (2n words), x for 2, 3 and 4;
+ * out1 is written for 1 and 5.  n is in [1, 2^24].  Test support; no
+ * counterpart in the reference. */
+int nt_math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x, double* out0,
+                 double* out1);
+
 #ifdef __cplusplus
 }
 #endif

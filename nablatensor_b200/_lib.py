@@ -116,6 +116,8 @@ SIGNATURES = {
     "nt_fma_peak": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
     "nt_fma_peak_sustained": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
     "nt_math_probe": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
+    "nt_math_eval": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint32), _f64p, _f64p,
+                      _f64p], ctypes.c_int),
     "nt_replay_noalloc": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
                            ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
@@ -130,6 +132,23 @@ def math_probe(device: int, which: int, iters: int) -> float:
     out = ctypes.c_double(0.0)
     check(lib().nt_math_probe(device, which, iters, ctypes.byref(out)))
     return out.value
+
+
+def math_eval(device: int, which: int, words=None, x=None):
+    """nt_math_eval: one of the replay's fp64 routines on the device over the
+    given generator words (which 0, 1, 5) or arguments (2, 3, 4).  Returns
+    out0, or (out0, out1) for which 1 and 5."""
+    import numpy as np
+    w = None if words is None else np.ascontiguousarray(words, dtype=np.uint32)
+    a = None if x is None else np.ascontiguousarray(x, dtype=np.float64)
+    n = (len(w) // 2 if which == 5 else len(w)) if w is not None else len(a)
+    out0 = np.empty(n, dtype=np.float64)
+    out1 = np.empty(n, dtype=np.float64) if which in (1, 5) else None
+    check(lib().nt_math_eval(device, which, n,
+                             None if w is None else w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+                             None if a is None else a.ctypes.data_as(_f64p),
+                             out0.ctypes.data_as(_f64p), None if out1 is None else out1.ctypes.data_as(_f64p)))
+    return out0 if out1 is None else (out0, out1)
 
 
 def fma_peak(device: int = 0, fp64: bool = True, iters: int = 4096) -> float:

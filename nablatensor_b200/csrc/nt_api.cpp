@@ -251,6 +251,11 @@ extern "C" int nt_math_probe(int32_t device, int32_t which, int32_t iters, doubl
   });
 }
 
+extern "C" int nt_math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x,
+                            double* out0, double* out1) {
+  return guarded([&] { nt::math_eval(device, which, n, words, x, out0, out1); });
+}
+
 extern "C" int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops) {
   return guarded([&] {
     if (!tflops) nt::fail(NT_E_INVALID_ARG, "tflops is null");

@@ -47,6 +47,16 @@ typedef unsigned long long nt_u64;
 #define NT_UINT_SCALE 2.3283064365386963e-10
 #define NT_TWO_PI 6.283185307179586
 
+/* The reference's Box-Muller angle theta = fl(2 pi u2): the product is
+ * rounded on its own, never fused into the subtraction that reduces it (a
+ * contracted fma would take sin of the unrounded product, up to 4 ulp away
+ * from the reference's normals). */
+#ifdef NT_HOST
+#define NT_THETA(u2) (NT_TWO_PI * (u2))
+#else
+#define NT_THETA(u2) __dmul_rn(NT_TWO_PI, (u2))
+#endif
+
 /* Per-(path, seed, stream) key words. */
 struct nt_key {
   nt_u32 lo;
@@ -187,7 +197,7 @@ NT_FN double nt_neg2log_u1(nt_u32 w0) {
  * Taylor series on |x| <= pi/4 to x^17 (sin) and x^16 (cos). */
 NT_FN void nt_sincos_2pi_u2(nt_u32 w1, double* sn, double* cs) {
   const double u2 = ((double)w1 + 0.5) * NT_UINT_SCALE;
-  const double th = NT_TWO_PI * u2;
+  const double th = NT_THETA(u2);
 #ifdef NT_HOST
   const int k = (int)nearbyint(th * 0.6366197723675814);
 #else
@@ -437,7 +447,7 @@ NT_FN double nt_neg2log_u1_t(nt_u32 w0) {
  * rounding; sin b to b^7 and cos b - 1 to b^6 (truncation < 2^-61). */
 NT_FN void nt_sincos_2pi_u2_t(nt_u32 w1, double* sn, double* cs) {
   const double u2 = fma((double)w1, 0x1p-32, 0x1p-33); /* (w1 + 0.5) 2^-32, exact */
-  const double th = NT_TWO_PI * u2;
+  const double th = NT_THETA(u2);
   const int j = (int)(w1 >> 24);
   double S, C;
   nt_tab2(NT_SC_TAB, j, &S, &C);

@@ -166,6 +166,8 @@ extern const double kFlopWeights[4];
 
 // Math probe launches (per-call counts under ncu).
 void math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
+void math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x, double* out0,
+               double* out1);
 
 // Vector-FMA peak (TFLOP/s) measured with independent FMA chains: a burst
 // (best of a few short launches) and a sustained rate (launches back to back

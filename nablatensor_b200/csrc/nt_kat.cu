@@ -143,6 +143,78 @@ void math_probe(int32_t device, int32_t which, int32_t iters, double* checksum) 
 
 }  // namespace nt
 
+// ---- the dedicated routines over given inputs (accuracy tests) -----------------
+
+namespace {
+
+__global__ void math_eval_kernel(int which, long long n, const unsigned* words, const double* x, double* out0,
+                                 double* out1) {
+  nt_math_tables_load();  // every thread, before the bounds check
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  switch (which) {
+    case 0: out0[i] = nt_neg2log_u1_t(words[i]); break;
+    case 1: nt_sincos_2pi_u2_t(words[i], &out0[i], &out1[i]); break;
+    case 2: out0[i] = nt_sqrt_pos(x[i]); break;
+    case 3: out0[i] = nt_exp_small(x[i]); break;
+    case 4: out0[i] = nt_exp_cw(x[i]); break;
+    case 5: nt_bm64_words(words[2 * i], words[2 * i + 1], &out0[i], &out1[i]); break;
+    default: break;
+  }
+}
+
+}  // namespace
+
+namespace nt {
+
+void math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x, double* out0,
+               double* out1) {
+  if (which < 0 || which > 5) fail(NT_E_INVALID_ARG, "which must be in [0, 5]");
+  if (n < 1 || n > (1ll << 24)) fail(NT_E_INVALID_ARG, "n must be in [1, 2^24]");
+  const bool use_words = which == 0 || which == 1 || which == 5;
+  const bool two_out = which == 1 || which == 5;
+  const int64_t n_words = which == 5 ? 2 * n : n;
+  if (!out0 || (two_out && !out1) || (use_words && !words) || (!use_words && !x))
+    fail(NT_E_INVALID_ARG, "a required array is null");
+  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  unsigned* d_w = nullptr;
+  double *d_x = nullptr, *d_o0 = nullptr, *d_o1 = nullptr;
+  cudaStream_t s = nullptr;
+  cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+  try {
+    if (use_words) {
+      cuda_check(cudaMalloc(&d_w, n_words * sizeof(unsigned)), "cudaMalloc");
+      cuda_check(cudaMemcpyAsync(d_w, words, n_words * sizeof(unsigned), cudaMemcpyHostToDevice, s), "copy in");
+    } else {
+      cuda_check(cudaMalloc(&d_x, n * sizeof(double)), "cudaMalloc");
+      cuda_check(cudaMemcpyAsync(d_x, x, n * sizeof(double), cudaMemcpyHostToDevice, s), "copy in");
+    }
+    cuda_check(cudaMalloc(&d_o0, n * sizeof(double)), "cudaMalloc");
+    if (two_out) cuda_check(cudaMalloc(&d_o1, n * sizeof(double)), "cudaMalloc");
+    const unsigned threads = 256;
+    const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+    math_eval_kernel<<<blocks, threads, 0, s>>>(which, n, d_w, d_x, d_o0, d_o1);
+    cuda_check(cudaGetLastError(), "math_eval_kernel launch");
+    cuda_check(cudaMemcpyAsync(out0, d_o0, n * sizeof(double), cudaMemcpyDeviceToHost, s), "copy out");
+    if (two_out) cuda_check(cudaMemcpyAsync(out1, d_o1, n * sizeof(double), cudaMemcpyDeviceToHost, s), "copy out");
+    cuda_check(cudaStreamSynchronize(s), "math_eval_kernel");
+  } catch (...) {
+    cudaFree(d_w);
+    cudaFree(d_x);
+    cudaFree(d_o0);
+    cudaFree(d_o1);
+    cudaStreamDestroy(s);
+    throw;
+  }
+  cudaFree(d_w);
+  cudaFree(d_x);
+  cudaFree(d_o0);
+  cudaFree(d_o1);
+  cudaStreamDestroy(s);
+}
+
+}  // namespace nt
+
 // ---- fp64 / fp32 vector-FMA peak ------------------------------------------------
 //
 // The roofline denominator for the replay kernels: MEASURED_PEAKS.json holds
