@@ -265,11 +265,13 @@ NT_FN double nt_exp_small(double x) {
 /* exp(x) over the whole double range, without a branch (Cody and Waite 1980):
  * k = rint(x / ln2) by the rounding constant 1.5 * 2^52, r = x - k ln2 with
  * ln2 in two parts (the high part has 42 significant bits, so k * hi is exact
- * for |k| < 2^11), |r| <= ln2 / 2, exp(r) by its Taylor series to r^13
- * (truncation < 2^-57), then scaled by 2^(k/2) * 2^(k - k/2), each factor a
- * normal power of two, so the overflow threshold and gradual underflow round
- * once.  x is clamped to [-746, 710] first (exp is 0 or infinite beyond);
- * NaN passes through. */
+ * for |k| < 2^11), |r| <= ln2 / 2; exp(r) = 1 + r (1 + r q(r)) with q the
+ * degree-9 Chebyshev interpolant of (e^r - 1 - r) / r^2 on the reduced range
+ * (nt_math_tables.cuh; 1.6e-17 relative, 11 FMAs where the Taylor series to
+ * r^13 took 13); then scaled by 2^(k/2) * 2^(k - k/2), each factor a normal
+ * power of two, so the overflow threshold and gradual underflow round once.
+ * x is clamped to [-746, 710] first (exp is 0 or infinite beyond); NaN
+ * passes through. */
 NT_FN double nt_exp_cw(double x) {
   const double xc = fmin(fmax(x, -746.0), 710.0);
   const double kt = fma(xc, 0x1.71547652b82fep+0 /* 1/ln2 */, 0x1.8p52);
@@ -277,20 +279,17 @@ NT_FN double nt_exp_cw(double x) {
   const int k = (int)nt_loword(kt);
   double r = fma(kd, -0x1.62e42fefa3800p-1 /* ln2 hi */, xc);
   r = fma(kd, -0x1.ef35793c76730p-45 /* ln2 lo */, r);
-  double p = 1.0 / 6227020800.0;       /* 1/13! */
-  p = fma(p, r, 1.0 / 479001600.0);    /* 1/12! */
-  p = fma(p, r, 1.0 / 39916800.0);     /* 1/11! */
-  p = fma(p, r, 1.0 / 3628800.0);      /* 1/10! */
-  p = fma(p, r, 1.0 / 362880.0);
-  p = fma(p, r, 1.0 / 40320.0);
-  p = fma(p, r, 1.0 / 5040.0);
-  p = fma(p, r, 1.0 / 720.0);
-  p = fma(p, r, 1.0 / 120.0);
-  p = fma(p, r, 1.0 / 24.0);
-  p = fma(p, r, 1.0 / 6.0);
-  p = fma(p, r, 0.5);
-  p = fma(p, r, 1.0);
-  p = fma(p, r, 1.0);
+  double q = NT_EXPW_C9;
+  q = fma(q, r, NT_EXPW_C8);
+  q = fma(q, r, NT_EXPW_C7);
+  q = fma(q, r, NT_EXPW_C6);
+  q = fma(q, r, NT_EXPW_C5);
+  q = fma(q, r, NT_EXPW_C4);
+  q = fma(q, r, NT_EXPW_C3);
+  q = fma(q, r, NT_EXPW_C2);
+  q = fma(q, r, NT_EXPW_C1);
+  q = fma(q, r, NT_EXPW_C0);
+  const double p = fma(fma(q, r, 1.0), r, 1.0);
   const int k1 = k >> 1, k2 = k - k1;
   const double y = (p * nt_from_words((k1 + 1023) << 20, 0u)) * nt_from_words((k2 + 1023) << 20, 0u);
   return x != x ? x : y;
