@@ -1,6 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: replay of the fp64 252-step Asian-call valuation tape with value
-+ 5 Greeks from one adjoint sweep, 1e9 scenarios per step,
++ 5 Greeks from one adjoint sweep, 1e9 scenarios per step (benchmark
+configuration 3, the headline),
 scenario ranges sharded across the GPUs with one NCCL all-reduce of the
 7 fp64 accumulators.
 
@@ -8,8 +9,8 @@ scenario ranges sharded across the GPUs with one NCCL all-reduce of the
                     [--workload asian1e9|asian2m|barrier20m|basket10m|cva1m]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-The default workload is config 3 above; `--workload` times the other
-BASELINE configurations (1: Asian 2M, 2: fp32 barrier 20M, 4: 10-asset
+The default workload is configuration 3 above; `--workload` times the other
+benchmark configurations (1: Asian 2M, 2: fp32 barrier 20M, 4: 10-asset
 basket 10M, 5: CVA of a 100-swap book 1M) with the same JSON line.
 
 Prints one JSON line on rank 0.  `value` is whole-job scenarios/s timed with
@@ -47,7 +48,7 @@ L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
 class Workload:
-    """One BASELINE configuration: the tape, its inputs, precision and size.
+    """One benchmark configuration: the tape, its inputs, precision and size.
     `cpu_share` scales the CPU sample so each workload's CPU leg does about
     the same amount of interpreter work (the basket tape is ~8x the Asian)."""
 
@@ -481,7 +482,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="asian1e9",
-                    help="BASELINE configuration to time (default: config 3, the headline)")
+                    help="benchmark configuration to time (default: configuration 3, the headline)")
     ap.add_argument("--paths", type=float, default=None, help="scenarios per step (default: the workload's)")
     ap.add_argument("--chunk", type=int, default=None, help="scenarios per launch (default: the workload's)")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000)

@@ -308,8 +308,9 @@ void reverse_reads(const Loop& lp, int32_t j, std::vector<Ref>& out) {
   }
 }
 
-// Algorithmic flop weights per op (frozen; see DESIGN.md "flop convention").
-// Transcendentals count the fp64 flops of the device routine (FMA = 2).
+// Algorithmic flop weights per op, frozen: an arithmetic op is 1 flop, an
+// adjoint contribution d += dy*v is 2.  Transcendentals count the fp64 flops
+// of the library routine measured once on the device (FMA = 2, nt_flops.cpp).
 struct Weights {
   double add = 1, mul = 1, div = 1, neg = 1, minmax = 1, abs = 1;
   double exp = 0, log = 0, sqrt = 0, sincos = 0;  // filled from kFlopWeights

@@ -279,7 +279,7 @@ class BasketOption:
 
 
 def basket_config4_market(n: int = 10, seed: int = 7):
-    """BASELINE config 4 market: spots ~ U[80, 120] and vols ~ U[0.15, 0.40],
+    """Benchmark configuration 4's market: spots ~ U[80, 120] and vols ~ U[0.15, 0.40],
     drawn with numpy's PCG64 generator seeded 7 (spots first, then vols)."""
     g = np.random.Generator(np.random.PCG64(seed))
     spots = g.uniform(80.0, 120.0, n)
@@ -289,7 +289,7 @@ def basket_config4_market(n: int = 10, seed: int = 7):
 
 def basket_tape(n: int = 10, steps: int = 52, rho: float = 0.5, seed: int = 7, strike: float = 100.0,
                 rate: float = 0.03, maturity: float = 1.0) -> AadTape:
-    """10-asset equal-weight basket call, equicorrelation
+    """Benchmark configuration 4: 10-asset equal-weight basket call, equicorrelation
     0.5, 52 weekly steps, T = 1; 21 Greeks (10 spots, 10 vols, rate)."""
     spots, vols = basket_config4_market(n, seed)
     return AadRecorder.record(lambda rec: BasketOption.record(
@@ -322,7 +322,7 @@ def barrier_tape(steps: int = 252, level: float = 80.0, width: float = 1.0, kind
 # The reference records CVA path by path and trade by trade
 # (nablatensor-cva/.../ExposureSimulation.java:121-229, InterestRateSwap.java:129-154,
 # HwShortRate.java): every exposure date values each swap's remaining coupons, so
-# no two dates record the same nodes.  The book here is the BASELINE config-5
+# no two dates record the same nodes.  The book here is the benchmark configuration 5
 # book -- 100 spot-starting payer swaps on a semi-annual grid, a 40-pillar zero
 # curve -- and its netted value is the same sum regrouped by payment date, so
 # every monthly date records one identical body and only its constants change
@@ -382,7 +382,7 @@ def _curve_weights(t: float, tenors: Sequence[float]) -> np.ndarray:
 def cva_tape(dates: int = 120, horizon: float = 10.0, a: float = 0.05, sigma: float = 0.01, hazard: float = 0.02,
              recovery: float = 0.4, book: SwapBook = None, pillars: int = 40, seed: int = 11,
              accrual: float = 0.5) -> AadTape:
-    """CVA of the swap book, adjoints w.r.t. the pillar zero
+    """Benchmark configuration 5: CVA of the swap book, adjoints w.r.t. the pillar zero
     rates and the hazard rate (41 inputs)."""
     book = book if book is not None else SwapBook.config5(seed=seed, accrual=accrual)
     tenors, zeros = cva_config5_curve(pillars, seed)

@@ -125,7 +125,7 @@ def test_fp32_host_build_tracks_the_fp32_oracle(oracle_mod):
 
 @pytest.mark.parametrize("n,steps", [(3, 8), (4, 5)])
 def test_correlated_basket(oracle_mod, n, steps):
-    """BASELINE config 4's shape (Cholesky mix of n normals per step, n GBM
+    """Benchmark configuration 4's shape (Cholesky mix of n normals per step, n GBM
     assets, 2n + 1 inputs) at a size the host runs quickly."""
     tape = quant.basket_tape(n=n, steps=steps)
     _run(oracle_mod, tape, tape.recordedInputs(), 2_000, 5, 7)
@@ -152,7 +152,7 @@ def test_loop_with_gathered_inputs(oracle_mod, steps):
 
 
 def test_cva_book_is_bit_exact(oracle_mod):
-    """BASELINE config 5's shape at a size the host runs quickly: 24 monthly
+    """Benchmark configuration 5's shape at a size the host runs quickly: 24 monthly
     dates over two years, 10 swaps; the per-date constants (live coupons,
     bond coefficients, curve weights) vary from unit to unit."""
     book = quant.SwapBook.config5(n=10)

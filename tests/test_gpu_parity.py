@@ -7,7 +7,7 @@ Tolerances (stated by the task and the reference's own tests):
                      remaining difference is the device's reduction order
                      and its libm's last-ulp differences.
   loop vs straight   2e-12 (CudaCheckpointParityTest.java:126 fp64 bound)
-  fp32 kernel        price within 1e-5 of the fp64 oracle (BASELINE), Greeks
+  fp32 kernel        price within 1e-5 of the fp64 oracle (the benchmark's bound), Greeks
                      within the fp32 oracle's own distance from fp64 plus 1e-5
                      (measured in test_barrier_fp32_against_fp64_oracle).
 """
@@ -225,7 +225,7 @@ def test_general_tapes_fp64(engine, oracle_mod, make, inputs, seed):
 
 
 def test_basket_config4_fp64(engine, oracle_mod):
-    """10-asset basket, 52 weekly steps, 21 Greeks."""
+    """Benchmark configuration 4: 10-asset basket, 52 weekly steps, 21 Greeks."""
     tape = quant.basket_tape()
     assert tape.input_count() == 21
     one = FP64.with_engine_option("cuda", "segUnits", "1")
@@ -258,7 +258,7 @@ def test_wide_exp_arguments_take_the_guarded_redo(engine, oracle_mod, vol, steps
 
 
 def test_cva_config5_fp64(engine, oracle_mod):
-    """CVA of 100 payer swaps under Hull-White, 120 monthly
+    """Benchmark configuration 5: CVA of 100 payer swaps under Hull-White, 120 monthly
     dates; adjoints w.r.t. the 40 pillar zero rates and the hazard rate.  The
     loop's per-date constants come from the per-unit table and each date's
     curve value is gathered from before the loop."""
@@ -361,7 +361,7 @@ def test_no_spill_and_plan(engine):
 
 
 def test_barrier_fp32_reproduces_the_fp32_oracle(engine, oracle_mod):
-    """fp32 kernel (BASELINE config 2 tape, 200k paths).  The reference's fp32
+    """fp32 kernel (benchmark configuration 2 tape, 200k paths).  The reference's fp32
     semantics store every node in float but evaluate transcendentals in double
     (ScalarReplay.java:37-51); the kernel does the same and must reproduce the
     oracle's fp32 mode to 1e-6 per channel.  Against the fp64 oracle it then
