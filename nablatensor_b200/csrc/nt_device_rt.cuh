@@ -296,23 +296,26 @@ NT_FN double nt_exp_cw(double x) {
 }
 
 /* sqrt of a positive normal argument (the Box-Muller radius, in
- * (4.6e-10, 46.1)): the hardware reciprocal square-root approximation as the
- * seed, one Newton step on it, and one residual correction of the root
- * (Markstein's method), which squares the remaining relative error.  Measured
- * on the device against long-double sqrt (tests/test_gpu_math.py): 0.5 ulp
- * worst over 5M arguments, i.e. correctly rounded; a second Newton step
- * changed no result and cost 3 % of the replay's speed. */
+ * (4.6e-10, 46.1)): the hardware reciprocal square-root approximation y as
+ * the seed; the root g = a y and the half reciprocal h = y / 2 refined
+ * together by one coupled Newton step (Goldschmidt's iteration), then one
+ * residual correction of the root (Markstein's method), which squares the
+ * remaining relative error: 7 fp64 operations.  Measured on the device
+ * against long-double sqrt (tests/test_gpu_math.py): 0.5 ulp worst over 5M
+ * arguments, i.e. correctly rounded; a second Newton step changed no result
+ * and cost 3 % of the replay's speed. */
 NT_FN double nt_sqrt_pos(double a) {
 #ifdef NT_HOST
   return sqrt(a);
 #else
   double y;
   asm("rsqrt.approx.ftz.f64 %0, %1;" : "=d"(y) : "d"(a));
-  const double h = 0.5 * a;
-  const double e = fma(-h * y, y, 0.5);
-  y = fma(y, e, y);
-  const double s = a * y;
-  return fma(fma(-s, s, a), 0.5 * y, s);
+  double g = a * y;    /* sqrt(a) */
+  double h = 0.5 * y;  /* 1 / (2 sqrt(a)) */
+  const double r = fma(-g, h, 0.5);
+  g = fma(g, r, g);
+  h = fma(h, r, h);
+  return fma(fma(-g, g, a), h, g);
 #endif
 }
 
