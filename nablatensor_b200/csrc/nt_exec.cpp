@@ -237,17 +237,23 @@ void Exec::load(int max_regs) {
     if (p2.loop.present && p2.loop.G == 2) {
       c2.seg_units = cfg.seg_units;
       std::string s2 = emit(tape, p2, c2);
-      double secs2 = 0.0;
-      std::vector<char> bin2 = nvrtc_compile(s2, "sm_100a", use_disk_cache, &secs2, cfg.fmad, max_regs);
-      secs += secs2;
+      // The wider kernel is optional: if it fails to compile or load, the
+      // first one stays.
       CUmodule m2 = nullptr;
       CUfunction f2 = nullptr;
-      cu_check(d.moduleLoadData(&m2, bin2.data()), "cuModuleLoadData");
-      cu_check(d.moduleGetFunction(&f2, m2, "nt_replay_kernel"), "cuModuleGetFunction");
-      int regs2 = 0, local2 = 0;
-      cu_check(d.funcGetAttribute(&regs2, CU_FUNC_ATTRIBUTE_NUM_REGS, f2), "cuFuncGetAttribute");
-      cu_check(d.funcGetAttribute(&local2, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f2), "cuFuncGetAttribute");
-      if (regs2 < 255 && local2 == 0) {
+      int regs2 = 255, local2 = 1;
+      try {
+        double secs2 = 0.0;
+        std::vector<char> bin2 = nvrtc_compile(s2, "sm_100a", use_disk_cache, &secs2, cfg.fmad, max_regs);
+        secs += secs2;
+        cu_check(d.moduleLoadData(&m2, bin2.data()), "cuModuleLoadData");
+        cu_check(d.moduleGetFunction(&f2, m2, "nt_replay_kernel"), "cuModuleGetFunction");
+        cu_check(d.funcGetAttribute(&regs2, CU_FUNC_ATTRIBUTE_NUM_REGS, f2), "cuFuncGetAttribute");
+        cu_check(d.funcGetAttribute(&local2, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f2), "cuFuncGetAttribute");
+      } catch (const Error&) {
+        regs2 = 255;
+      }
+      if (m2 && regs2 < 255 && local2 == 0) {
         cu_check(d.moduleUnload(module), "cuModuleUnload");
         module = m2;
         function = f2;
@@ -255,7 +261,7 @@ void Exec::load(int max_regs) {
         source = std::move(s2);
         regs = regs2;
         local = local2;
-      } else {
+      } else if (m2) {
         cu_check(d.moduleUnload(m2), "cuModuleUnload");
       }
     }
