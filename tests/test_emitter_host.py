@@ -190,3 +190,24 @@ def test_power_of_two_divisions_become_exact_multiplications(oracle_mod, f32):
     src = _run(oracle_mod, tape, [1.5, 0.3], 500, 7, 42, f32=f32, flags=_lib.NT_FLAG_NO_LOOP)
     # straight-line code: the 2 kept divisions per step, and their d/vb rules
     assert sum(line.count(" / ") for line in src.splitlines()) == 4 * steps
+
+
+def test_power_of_two_constant_shared_by_divisions_and_kept_when_used_otherwise(oracle_mod):
+    """A constant 4 that only divides (twice) is rewritten once for both
+    divisions; a constant 8 that divides and is also an output stays a
+    division; 2^1023 (reciprocal subnormal) stays a division."""
+    from nablatensor_b200.tape import AadRecorder
+
+    def body(rec):
+        s = rec.input("s", 1.5)
+        four = rec.constant(4.0)
+        eight = rec.constant(8.0)
+        big = rec.constant(2.0 ** 1023)
+        z = rec.randn()
+        y = s.div(four).add(z.div(four)).add(s.div(eight)).add(s.div(big).mul(2.0 ** 1000))
+        rec.output("y", y)
+        rec.output("eight", eight)
+    tape = AadRecorder.record(body)
+    src = _run(oracle_mod, tape, [1.5], 1_000, 3, 42, flags=_lib.NT_FLAG_NO_LOOP)
+    fwd = [line for line in src.splitlines() if "const real v" in line and " / " in line]
+    assert len(fwd) == 2  # s / 8 and s / 2^1023; both divisions by 4 became multiplications
