@@ -277,10 +277,10 @@ int nt_replay_sharded(nt_exec* exec, uint64_t total_paths, uint64_t path_offset,
 
 /*
  * nt_replay without any allocation, for callers that cannot let the engine
- * allocate device memory: a host that captures its pricing loop into a CUDA
- * graph (cudaMalloc/cudaFree cannot be captured), or one that hands the whole
- * device to its own memory pool under a fixed budget.  No counterpart in the
- * reference.
+ * allocate device memory: a host that hands the whole device to its own
+ * memory pool under a fixed budget, or one pricing inside a latency-critical
+ * loop, where cudaMalloc/cudaFree would synchronise the device.  No
+ * counterpart in the reference.
  *
  * Launches `exec`'s kernel on the caller's stream (a cudaStream_t, NULL for
  * the legacy default stream) over [path_offset, path_offset + paths), reading

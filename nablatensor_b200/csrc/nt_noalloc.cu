@@ -1,12 +1,13 @@
 // nt_noalloc.cu -- a replay launch that allocates nothing.
 //
 // Some callers cannot let the engine allocate device memory on their behalf:
-// a host that captures its pricing loop into a CUDA graph (cudaMalloc and
-// cudaFree are not stream operations and cannot be captured), and a host
-// that hands the whole device to its own memory pool under a fixed budget,
-// as NablaTensor's Java runtime pools and budgets every device allocation.
-// For them nt_replay_noalloc launches an already-compiled replay kernel on
-// the caller's own device buffers and stream.  The kernel's only scratch --
+// a host that hands the whole device to its own memory pool under a fixed
+// budget (NablaTensor's Java runtime pools and budgets every device
+// allocation, so memory taken behind its back breaks its accounting), and a
+// host pricing inside a latency-critical loop, where cudaMalloc and cudaFree
+// would synchronise the device.  For them nt_replay_noalloc launches an
+// already-compiled replay kernel on the caller's own device buffers and
+// stream.  The kernel's only scratch --
 // one partial record per block and the reduction ticket -- lives in the
 // file-scope array below, of a fixed maximum size that every GPU loading this
 // library holds until the process exits.

@@ -1,7 +1,8 @@
 """nt_replay_noalloc: the replay launch for callers that cannot allocate.
 
-A host that captures its pricing loop into a CUDA graph, or that hands the
-whole device to its own memory pool, cannot let the engine call cudaMalloc.
+A host that hands the whole device to its own budgeted memory pool, or that
+prices inside a latency-critical loop where cudaMalloc and cudaFree would
+synchronise the device, cannot let the engine allocate.
 nt_replay_noalloc runs an already-compiled kernel on the caller's device
 buffers and stream, with its reduction scratch in a static device array.
 Here it must give the same sums as nt_replay (the existing entry point) on
