@@ -349,8 +349,8 @@ int nt_fma_peak_sustained(int32_t device, int32_t fp64, int32_t millis, double* 
  * 1 library exp, 2 library log, 3 library sincos, 4 library sqrt, 5 the
  * replay's full-range exp, 6 its series -2 ln(u1), 7 its series sincos(2 pi u2),
  * 8 library exp on a wide range, 9 the table-driven -2 ln(u1), 10 the
- * table-driven sincos(2 pi u2), 11 the radius sqrt, 12 the Taylor-series
- * exp, 13 one Philox2x32-10 block.  No counterpart in the reference. */
+ * table-driven sincos(2 pi u2), 11 the radius sqrt, 12 the series exp
+ * (|x| <= 1/8), 13 one Philox2x32-10 block.  No counterpart in the reference. */
 int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 
 /* Evaluates one of the replay's dedicated fp64 routines on the device over n

@@ -125,7 +125,7 @@ SIGNATURES = {
 MATH_PROBES = {0: "loop", 1: "exp(lib, |x|<=1/8)", 2: "log(lib)", 3: "sincos(lib)", 4: "sqrt(lib)",
                5: "exp(full range)", 6: "-2ln(u1)(series)", 7: "sincos(2pi u2)(series)", 8: "exp(lib, |x|<=4)",
                9: "-2ln(u1)(table)", 10: "sincos(2pi u2)(table)", 11: "sqrt(replay radius)",
-               12: "exp(Taylor series)", 13: "philox2x32-10 block"}
+               12: "exp(series, |x|<=1/8)", 13: "philox2x32-10 block"}
 
 
 def math_probe(device: int, which: int, iters: int) -> float:

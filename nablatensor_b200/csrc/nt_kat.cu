@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256) math_probe_kernel(int which, int iters, d
       case 9: acc += nt_neg2log_u1_t(w); break;                       // table-driven -2 ln u1
       case 10: nt_sincos_2pi_u2_t(w, &s, &c); acc += s; acc2 += c; break;  // table-driven sincos
       case 11: acc += nt_sqrt_pos(u * 46.0); break;                   // the replay's radius sqrt
-      case 12: acc += nt_exp_small((u - 0.5) * 0.25); break;          // Taylor-series exp
+      case 12: acc += nt_exp_small((u - 0.5) * 0.25); break;          // series exp, |x| <= 1/8
       case 13: {                                                       // one Philox block
         nt_u32 a, b;
         nt_philox(w, (unsigned)i, &a, &b);
