@@ -181,3 +181,16 @@ def test_java_options_layout_follows_the_header():
         text = f.read()
     layout = re.search(r"StructLayout OPTIONS = MemoryLayout\.structLayout\((.*?)\);", text, re.S).group(1)
     assert re.findall(r'withName\("(\w+)"\)', layout) == _header_fields("nt_options")
+
+
+def test_math_eval_rejects_bad_arguments_before_touching_a_device(ntlib):
+    L = _lib.lib()
+    out = np.zeros(4)
+    x = np.zeros(4)
+    p = out.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+    xp = x.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+    assert L.nt_math_eval(0, 6, 4, None, xp, p, p) == _lib.NT_E_INVALID_ARG  # unknown routine
+    assert L.nt_math_eval(0, 2, 0, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # n < 1
+    assert L.nt_math_eval(0, 2, (1 << 24) + 1, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # n > 2^24
+    assert L.nt_math_eval(0, 0, 4, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # words needed
+    assert L.nt_math_eval(0, 1, 4, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # out1 needed
