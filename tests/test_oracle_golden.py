@@ -3,7 +3,9 @@
 Golden values (the reference's scalar `cpu` engine, JDK 25, 16 threads):
   G1  docs/validation.md:56-63             Asian call, 252 steps, 1,000,000 paths, seed 42
   G2  docs/examples/asian-greeks.md:43-46  the same at 2,000,000 paths (all engines agree)
-Both sit in tests/golden/reference_docs.json.  Reproducing them to every
+  G3  docs/validation.md:74-80             central bump-and-revalue of G1's market, relative
+                                           bump 5e-3 (BumpCrossCheck.java:40-44), same seed
+All sit in tests/golden/reference_docs.json.  Reproducing them to every
 printed digit needs all 2.5e8 generator draws, the Box-Muller legs, the
 1536-node forward sweep and the adjoint rules to be right.
 """
@@ -43,6 +45,29 @@ def test_g2_asian_2m_matches_asian_greeks_md(oracle_mod):
     g = _docs()["G2"]
     r = O.replay(O.asian_tape(252), ATM, 2_000_000, 0, 42)
     vals = {"price": r.value[0], "delta": r.gradients[0][0], "vega": r.gradients[0][2], "rho": r.gradients[0][3]}
+    for name, (want, digits) in g["values"].items():
+        _check_digits(vals[name], want, digits)
+
+
+def bump_greeks(price, x, rel):
+    """Central bump-and-revalue as the reference's cross-check does it
+    (BumpCrossCheck.java:40-44): h = rel * max(1, |x_j|), same seed."""
+    out = []
+    for j in range(len(x)):
+        h = rel * max(1.0, abs(x[j]))
+        up, dn = list(x), list(x)
+        up[j] += h
+        dn[j] -= h
+        out.append((price(up) - price(dn)) / (2 * h))
+    return out
+
+
+def test_g3_bump_cross_check_matches_validation_md(oracle_mod):
+    O = oracle_mod
+    g = _docs()["G3"]
+    t = O.asian_tape(252)
+    b = bump_greeks(lambda x: O.replay(t, x, g["paths"], 0, g["seed"]).value[0], ATM, g["relative_bump"])
+    vals = dict(zip(["delta", "dV/dK", "vega", "rho", "dV/dT"], b))
     for name, (want, digits) in g["values"].items():
         _check_digits(vals[name], want, digits)
 
@@ -122,3 +147,33 @@ def test_philox_fixture_matches_restatement(oracle_mod):
     for case in fx["cases"]:
         for q, pair in enumerate(case["words"]):
             assert tuple(pair) == O.normal_words(case["path"], case["seed"], case["stream"], case["pair0"] + q)
+
+
+# ExoticsTest (nablatensor-quant/.../ExoticsTest.java:30-95): the reference's own properties of the smoothed
+# barrier payoffs, at its sizes (64 steps, 200,000 paths, seed 12345).
+EXOTIC_STEPS, EXOTIC_PATHS, EXOTIC_SEED = 64, 200_000, 12345
+
+
+def test_knock_out_plus_knock_in_equals_vanilla(oracle_mod):
+    """ExoticsTest.knockOutPlusKnockInEqualsVanilla (:56-62): UP_OUT + UP_IN at
+    barrier 130, width 1 equals the European call to 1e-9 (1 + vanilla)."""
+    O = oracle_mod
+    price = lambda t: O.replay(t, ATM, EXOTIC_PATHS, 0, EXOTIC_SEED, adjoints=False).value[0]
+    out = price(O.barrier_tape(EXOTIC_STEPS, kind="UP_OUT", barrier=130.0, width=1.0))
+    inn = price(O.barrier_tape(EXOTIC_STEPS, kind="UP_IN", barrier=130.0, width=1.0))
+    vanilla = price(O.european_tape(EXOTIC_STEPS))
+    assert abs(vanilla - (out + inn)) <= 1e-9 * (1 + vanilla)
+    assert 0 < out < vanilla
+
+
+def test_barrier_adjoint_delta_matches_a_bump(oracle_mod):
+    """ExoticsTest.barrierAdjointDeltaMatchesABumpOfTheSmoothedPayoff (:81-94):
+    UP_OUT at 125, width 1.5, central bump h = 0.5 of the spot."""
+    O = oracle_mod
+    t = O.barrier_tape(EXOTIC_STEPS, kind="UP_OUT", barrier=125.0, width=1.5)
+    adj = O.replay(t, ATM, EXOTIC_PATHS, 0, EXOTIC_SEED).gradients[0][0]
+    h = 0.5
+    up = O.replay(t, [100.0 + h] + ATM[1:], EXOTIC_PATHS, 0, EXOTIC_SEED, adjoints=False).value[0]
+    dn = O.replay(t, [100.0 - h] + ATM[1:], EXOTIC_PATHS, 0, EXOTIC_SEED, adjoints=False).value[0]
+    fd = (up - dn) / (2 * h)
+    assert abs(fd - adj) <= 5e-3 + 5e-3 * abs(fd)
