@@ -138,6 +138,50 @@ def test_g1_golden_on_the_gpu(engine):
         assert abs(got - want) <= 6e-11 * abs(want)
 
 
+def test_g3_bump_cross_check_on_the_gpu(engine):
+    """docs/validation.md:74-80: central bump-and-revalue of the G1 market
+    (h = 5e-3 max(1, |x|), same seed, BumpCrossCheck.java:40-44) through
+    setInputs on one compiled executable, to the printed 9 digits."""
+    with open(os.path.join(GOLDEN, "reference_docs.json")) as f:
+        g = json.load(f)["G3"]
+    with engine.compile(quant.asian_tape(252), FP64) as ex:
+        def price(x):
+            ex.setInputs(x)
+            return ex.replay(g["paths"], 0, g["seed"]).value()
+        bumps = []
+        for j in range(5):
+            h = g["relative_bump"] * max(1.0, abs(ATM[j]))
+            up, dn = list(ATM), list(ATM)
+            up[j] += h
+            dn[j] -= h
+            bumps.append((price(up) - price(dn)) / (2 * h))
+    for got, name in zip(bumps, ["delta", "dV/dK", "vega", "rho", "dV/dT"]):
+        want, digits = g["values"][name]
+        tol = 0.5 * 10 ** (np.floor(np.log10(abs(want))) - (digits - 1))
+        assert abs(got - want) <= tol * 1.0000001, (name, got, want)
+
+
+def test_exotics_in_out_parity_and_bumped_delta_on_the_gpu(engine):
+    """ExoticsTest.java:56-62 and :81-94 on the GPU: UP_OUT + UP_IN (barrier
+    130, width 1) equals the European call to 1e-9 (1 + vanilla); the UP_OUT
+    (125, width 1.5) adjoint delta matches a central spot bump of 0.5."""
+    paths, seed = 200_000, 12345
+
+    def run(tape, x=ATM):
+        with engine.compile(tape, FP64) as ex:
+            ex.setInputs(x)
+            return ex.replay(paths, 0, seed)
+    out = run(quant.barrier_tape(64, level=130.0, width=1.0, kind=quant.Barrier.UP_OUT)).value()
+    inn = run(quant.barrier_tape(64, level=130.0, width=1.0, kind=quant.Barrier.UP_IN)).value()
+    vanilla = run(quant.european_tape(64)).value()
+    assert abs(vanilla - (out + inn)) <= 1e-9 * (1 + vanilla)
+    assert 0 < out < vanilla
+    t = quant.barrier_tape(64, level=125.0, width=1.5, kind=quant.Barrier.UP_OUT)
+    adj = run(t).gradients()[0]
+    fd = (run(t, [100.5] + ATM[1:]).value() - run(t, [99.5] + ATM[1:]).value()) / 1.0
+    assert abs(fd - adj) <= 5e-3 + 5e-3 * abs(fd)
+
+
 def test_1m_against_oracle_exact(engine, oracle_mod):
     tape = quant.asian_tape(252)
     with engine.compile(tape, FP64) as ex:
