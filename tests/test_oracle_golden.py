@@ -177,3 +177,45 @@ def test_barrier_adjoint_delta_matches_a_bump(oracle_mod):
     dn = O.replay(t, [100.0 - h] + ATM[1:], EXOTIC_PATHS, 0, EXOTIC_SEED, adjoints=False).value[0]
     fd = (up - dn) / (2 * h)
     assert abs(fd - adj) <= 5e-3 + 5e-3 * abs(fd)
+
+
+# MvpPricingTest (nablatensor-quant/.../MvpPricingTest.java:33-112): 400,000 scenarios, seed 20260830.
+MVP_PATHS, MVP_SEED = 400_000, 20260830
+
+
+def black_scholes_call(s, k, vol, r, t):
+    """Closed-form European call and its first-order Greeks (spot, strike,
+    vol, rate), the reference's BlackScholes.of(CALL, market)."""
+    import math
+    n = lambda x: 0.5 * (1.0 + math.erf(x / math.sqrt(2.0)))
+    d1 = (math.log(s / k) + (r + 0.5 * vol * vol) * t) / (vol * math.sqrt(t))
+    d2 = d1 - vol * math.sqrt(t)
+    df = math.exp(-r * t)
+    pdf = math.exp(-0.5 * d1 * d1) / math.sqrt(2.0 * math.pi)
+    return {"price": s * n(d1) - k * df * n(d2), "delta": n(d1), "dV/dK": -df * n(d2),
+            "vega": s * pdf * math.sqrt(t), "rho": k * t * df * n(d2)}
+
+
+MVP_TOLERANCE = {"price": 0.15, "delta": 0.02, "dV/dK": 0.02, "vega": 0.60, "rho": 0.60}
+
+
+def test_european_adjoint_greeks_match_black_scholes(oracle_mod):
+    """MvpPricingTest.europeanCallAdjointGreeksMatchBlackScholes (:37-53)."""
+    r = oracle_mod.replay(oracle_mod.european_tape(1), ATM, MVP_PATHS, 0, MVP_SEED)
+    g = r.gradients[0]
+    got = {"price": r.value[0], "delta": g[0], "dV/dK": g[1], "vega": g[2], "rho": g[3]}
+    ref = black_scholes_call(*ATM)
+    for name, tol in MVP_TOLERANCE.items():
+        assert abs(got[name] - ref[name]) <= tol, (name, got[name], ref[name])
+
+
+def test_asian_adjoint_delta_matches_a_bump(oracle_mod):
+    """MvpPricingTest.adjointGreeksMatchCentralBumpForAsian (:55-74): 64 steps,
+    h = 0.01 spot."""
+    O = oracle_mod
+    t = O.asian_tape(64)
+    adj = O.replay(t, ATM, MVP_PATHS, 0, MVP_SEED)
+    up = O.replay(t, [101.0] + ATM[1:], MVP_PATHS, 0, MVP_SEED, adjoints=False).value[0]
+    dn = O.replay(t, [99.0] + ATM[1:], MVP_PATHS, 0, MVP_SEED, adjoints=False).value[0]
+    assert abs((up - dn) / 2.0 - adj.gradients[0][0]) <= 5e-3
+    assert adj.value[0] > 0.0
