@@ -30,6 +30,7 @@ import argparse
 import ctypes
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -188,6 +189,7 @@ def cpu_compiled_baseline(wl: Workload, seconds: float = 5.0) -> dict:
                     "-fPIC", "-I", os.path.join(ROOT, "nablatensor_b200", "csrc"), "-o", so, cpp], check=True)
     build_s = time.perf_counter() - t0
     fn = ctypes.CDLL(so).nt_host_replay
+    shutil.rmtree(d, ignore_errors=True)  # the loaded library stays mapped
     fn.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
                    ctypes.POINTER(ctypes.c_double)]
     fn.restype = None
