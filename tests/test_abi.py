@@ -9,7 +9,7 @@ import pytest
 from nablatensor_b200 import _lib, quant
 from nablatensor_b200.tape import AadRecorder
 
-from tapes import every_op_tape, named_streams, multi_output
+from tapes import every_op_tape, multi_output, named_streams, nonuniform_asian, pow2_divisions, term_vol_asian
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -194,3 +194,20 @@ def test_math_eval_rejects_bad_arguments_before_touching_a_device(ntlib):
     assert L.nt_math_eval(0, 2, (1 << 24) + 1, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # n > 2^24
     assert L.nt_math_eval(0, 0, 4, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # words needed
     assert L.nt_math_eval(0, 1, 4, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # out1 needed
+
+
+@pytest.mark.parametrize("target", [0, 2])
+@pytest.mark.parametrize("make,opts", [
+    (lambda: quant.cva_tape(), {}),                      # gathered curve (shared memory), per-date table, carried leg
+    (term_vol_asian, {}),                                # gathered per-step inputs
+    (nonuniform_asian, {}),                              # per-unit constant table
+    (pow2_divisions, {}),                                # divisions rewritten as multiplications
+    (lambda: quant.basket_tape(), {"seg_units": 2}),     # the two-unit segment the engine may pick
+    (lambda: quant.asian_tape(252), {"rev_unroll": 2}),  # unrolled reverse segment loop
+])
+def test_plan_features_compile_for_sm100a(ntlib, make, opts, target):
+    """Every emission feature of the planner, for the single- and the
+    multi-market kernel, compiles with NVRTC for sm_100a."""
+    src = _lib.emit_source(make(), target=target, **opts)
+    assert ("nt_markets_kernel" if target == 2 else "nt_replay_kernel") in src
+    assert _lib.nvrtc_check(src) > 1000
