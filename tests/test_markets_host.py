@@ -17,7 +17,7 @@ from nablatensor_b200 import _lib, quant
 from oracle.oracle import FlatTape
 
 from conftest import host_kernel
-from tapes import every_op_tape, named_streams
+from tapes import every_op_tape, named_streams, nonuniform_asian, term_vol_asian
 
 ATM = [100.0, 100.0, 0.20, 0.03, 1.0]
 
@@ -75,3 +75,23 @@ def test_straight_line_and_streams(oracle_mod):
 
 def test_one_market_is_the_plain_replay(oracle_mod):
     _check(oracle_mod, quant.asian_tape(252), [ATM], 1_000, 0, 42)
+
+
+def test_per_unit_constants_and_gathered_inputs(oracle_mod):
+    """Loops whose units read a per-unit constant table or a node before the
+    loop chosen by the unit: each market gathers its own values."""
+    t = nonuniform_asian()
+    _check(oracle_mod, t, _markets(list(t.recordedInputs()), [(0, 1.0), (2, 1.3)]), 800, 3, 42)
+    t = term_vol_asian()
+    base = list(t.recordedInputs())
+    _check(oracle_mod, t, _markets(base, [(0, 1.0), (3, 1.5), (len(base) - 1, 0.7)]), 800, 5, 42)
+
+
+def test_cva_book_markets(oracle_mod):
+    """A small CVA book (24 monthly dates, 10 swaps) under a parallel and a
+    single-pillar curve bump and a hazard bump."""
+    t = quant.cva_tape(dates=24, horizon=2.0, book=quant.SwapBook.config5(n=10))
+    base = list(t.recordedInputs())
+    par = [x + 0.001 for x in base[:-1]] + [base[-1]]
+    mk = [base, par] + _markets(base, [(5, 1.1), (len(base) - 1, 1.5)])
+    _check(oracle_mod, t, mk, 300, 3, 11)
