@@ -211,3 +211,14 @@ def test_plan_features_compile_for_sm100a(ntlib, make, opts, target):
     src = _lib.emit_source(make(), target=target, **opts)
     assert ("nt_markets_kernel" if target == 2 else "nt_replay_kernel") in src
     assert _lib.nvrtc_check(src) > 1000
+
+
+def test_a_missing_library_fails_loudly_and_the_engine_reports_unavailable(monkeypatch):
+    """No fallback: without libnabla_b200.so every entry raises, and the SPI's
+    isAvailable() answers False without throwing (AadEngine.java:39-40)."""
+    from nablatensor_b200.engine import CudaAadEngine
+    monkeypatch.setattr(_lib, "LIB_PATH", os.path.join(ROOT, "no_such_dir", "libnabla_b200.so"))
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(RuntimeError, match="is missing"):
+        _lib.lib()
+    assert CudaAadEngine(0).isAvailable() is False
