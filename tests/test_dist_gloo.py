@@ -14,7 +14,6 @@ import socket
 import sys
 
 import numpy as np
-import pytest
 import torch.multiprocessing as mp
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
