@@ -82,7 +82,8 @@ typedef struct nt_tape {
                                     they are evaluated in fp64 and narrowed on store, the reference's
                                     fp32 semantics (ScalarReplay.java:37-51) */
 #define NT_FLAG_NO_FMAD 0x10     /* no multiply-add contraction (every product rounded) */
-#define NT_FLAG_ACC_REGS 0x20    /* keep the per-thread accumulators in registers, not shared memory */
+#define NT_FLAG_ACC_REGS 0x20    /* no effect: the per-thread accumulators it placed were replaced by
+                                    the exact per-warp accumulation; kept so old callers still compile */
 #define NT_FLAG_RECOMPUTE_ALL 0x40 /* reverse sweep recomputes every loop value from the step
                                       checkpoints (no per-thread value tape in global memory) */
 #define NT_FLAG_TAPE_DRAWS 0x80    /* tape only the draws and recompute exp/log/sqrt/div in the
@@ -180,6 +181,10 @@ int nt_set_inputs(nt_exec* exec, const double* inputs, int32_t n);
  * (the caller divides by `paths` and forms the standard error as
  * AadTotals.toResult does, AadTotals.java:68-89).  seconds (may be NULL)
  * receives the wall time of launch + synchronise + read-back.
+ * Each sum is the correctly rounded exact sum of per-tile sums, a tile being
+ * 32 consecutive scenarios from path_offset on; any split of the range into
+ * pieces that start on tile boundaries (nt_replay_accumulate chunks,
+ * nt_replay_sharded ranks) gives the same bits.
  * Replaces AadExecutable.replay (AadExecutable.java:46-47) as implemented by
  * DeviceAadExecutable.replay (DeviceAadExecutable.java:140-168).
  */
@@ -209,10 +214,11 @@ int nt_replay_markets(nt_exec* exec, int32_t n_states, const double* inputs, uin
 /*
  * Device-resident accumulation for long runs (the many-chunk replaySafe of
  * AbstractAadExecutable.java:101-121 without a read-back per chunk):
- * nt_replay_accumulate enqueues one dispatch that ADDS its sums into the
- * executable's device accumulator and returns without waiting;
- * nt_accumulator_read waits, copies the accumulator to `sums` and, when
- * reset != 0, zeroes it.
+ * nt_replay_accumulate enqueues one dispatch that ADDS its sums, exactly,
+ * into the executable's device accumulator and returns without waiting;
+ * nt_accumulator_read waits, rounds the accumulator into `sums` and, when
+ * reset != 0, zeroes it.  Chunks that start on 32-scenario tile boundaries
+ * of one range sum to the bits of one nt_replay over the whole range.
  */
 int nt_replay_accumulate(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed);
 int nt_accumulator_read(nt_exec* exec, double* sums, int32_t reset);
@@ -259,18 +265,25 @@ void nt_destroy(nt_exec* exec);
 int nt_dist_unique_id(uint8_t id[128]);
 
 /* Joins this executable to an nranks-wide NCCL communicator (one rank per
- * GPU, one process per rank).  timeout_ms bounds the join; on expiry the
- * communicator is aborted and NT_E_NCCL returned. */
+ * GPU, one process per rank; NCCL is loaded with dlopen, from
+ * $NT_NCCL_LIBRARY when set, else libnccl.so.2).  timeout_ms bounds the join
+ * and, later, each all-reduce once this rank's shard is done; on expiry or on
+ * an NCCL error the communicator is aborted (ncclCommAbort) and NT_E_NCCL
+ * returned, after which the executable is detached. */
 int nt_dist_attach(nt_exec* exec, int32_t nranks, int32_t rank, const uint8_t id[128],
                    int32_t timeout_ms);
 
 /*
  * Replays the global scenario range [path_offset, path_offset + total_paths)
- * with this rank's contiguous shard, then all-reduces the sums vector
- * (n_out * (2 + n_in) doubles) with one ncclAllReduce.  Every rank receives
- * the global sums.  chunk_paths > 0 splits this rank's shard into dispatches
- * of at most that many scenarios, accumulated on the device.
- * seconds (may be NULL) gets this rank's wall time of the call.
+ * with this rank's contiguous shard (nt_shard_range), then all-reduces the
+ * exact accumulator words (one int64 ncclAllReduce of n_out * (2 + n_in) x 69
+ * words).  Every rank receives the global sums, with the same bits as a
+ * single-GPU nt_replay of the whole range, whatever the number of ranks.
+ * chunk_paths > 0 splits this rank's shard into dispatches of at most that
+ * many scenarios (rounded down to a multiple of 32), accumulated on the
+ * device.  A peer that leaves or stalls ends the call with NT_E_NCCL within
+ * the attach timeout after this rank's shard is done.  seconds (may be NULL)
+ * gets this rank's wall time of the call.
  */
 int nt_replay_sharded(nt_exec* exec, uint64_t total_paths, uint64_t path_offset, uint64_t seed,
                       uint64_t chunk_paths, double* sums, double* seconds);
@@ -285,19 +298,23 @@ int nt_replay_sharded(nt_exec* exec, uint64_t total_paths, uint64_t path_offset,
  * Launches `exec`'s kernel on the caller's stream (a cudaStream_t, NULL for
  * the legacy default stream) over [path_offset, path_offset + paths), reading
  * the n_in input doubles from device memory `d_inputs` and writing the
- * n_out * (2 + n_in) sums (nt_replay's layout) to device memory `d_sums`.
- * Returns once the work is enqueued; synchronise the stream before reading.
- * Calls no cudaMalloc, cudaFree or other allocating routine.
+ * n_out * (2 + n_in) sums (nt_replay's layout and bits) to device memory
+ * `d_sums`; both must be device (or managed) memory of exec's GPU, else
+ * NT_E_INVALID_ARG.  Returns once the work is enqueued; synchronise the
+ * stream before reading.  Calls no cudaMalloc, cudaFree or other allocating
+ * routine.
  *
- * The kernel's reduction scratch lives in a static device array of 1 MiB that
- * every GPU loading the library holds until exit; a launch needing more
- * (blocks x channels x 8 bytes + 256) is rejected with NT_E_INVALID_ARG.
- * `exec` must be compiled with NT_FLAG_RECOMPUTE_ALL | NT_FLAG_SHARED_CKPT
- * (no value tape, no global checkpoints), else NT_E_UNSUPPORTED.  All calls
- * on a device share the scratch and keep the last call's contents: calls
- * that overlap on the GPU race.  The first call on each device looks up the
- * scratch address and zeroes it synchronously, so make it before any stream
- * capture.
+ * The kernel's reduction scratch lives in a static device array of 64 KiB
+ * that every GPU loading the library holds until exit; an executable needing
+ * more (256 + channels x 69 x 8 bytes, i.e. more than 118 channels, for
+ * example more than 116 inputs of a one-output tape) is rejected with
+ * NT_E_INVALID_ARG.  `exec` must have no value tape and no global
+ * checkpoints -- compile it with NT_FLAG_RECOMPUTE_ALL | NT_FLAG_SHARED_CKPT
+ * -- else NT_E_UNSUPPORTED.  All calls on a device share the scratch and
+ * keep the last call's contents (each call clears it on its stream first):
+ * calls that overlap on the GPU race.  The first call on each device looks up
+ * the scratch address (cudaGetSymbolAddress), so make it before any stream
+ * capture, and do not use the entry point across a cudaDeviceReset.
  */
 int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed, const double* d_inputs,
                       double* d_sums, void* stream);
@@ -312,8 +329,10 @@ int nt_replay_sharded_async(nt_exec* exec, uint64_t total_paths, uint64_t path_o
 int nt_dist_detach(nt_exec* exec);
 
 /* The contiguous shard of [path_offset, path_offset + total_paths) that rank
- * `rank` of `nranks` replays: the first total % nranks ranks take one extra
- * path.  Host arithmetic only (no device needed); nt_replay_sharded uses it. */
+ * `rank` of `nranks` replays: the range's ceil(total_paths / 32) tiles of 32
+ * scenarios are split into nranks contiguous runs, the first
+ * (tiles % nranks) runs one tile longer; a rank may get no scenario.  Host
+ * arithmetic only (no device needed); nt_replay_sharded uses it. */
 int nt_shard_range(uint64_t total_paths, uint64_t path_offset, int32_t nranks, int32_t rank, uint64_t* from,
                    uint64_t* count);
 

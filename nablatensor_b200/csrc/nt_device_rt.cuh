@@ -22,8 +22,9 @@
  *     nablatensor-core/.../CudaAadCodegen.java:485-510).
  *   - java.lang.Math.max/min semantics (NaN-propagating, -0 < +0), which the
  *     oracle uses (ScalarReplay.java:115-116).
- *   - the deterministic warp -> block -> grid reduction of the accumulators
- *     (atomic ticket, no spin-wait).
+ *   - the exact per-path accumulation: warp tiles of 32 paths summed into
+ *     fixed-point words (nt_exact.cuh), block words folded into the launch's
+ *     by atomics, the last block (atomic ticket, no spin-wait) rounding them.
  */
 #ifndef NT_DEVICE_RT_CUH
 #define NT_DEVICE_RT_CUH
@@ -35,6 +36,8 @@
 #else
 #define NT_FN static __device__ __forceinline__
 #endif
+
+#include "nt_exact.cuh"
 
 typedef unsigned int nt_u32;
 typedef unsigned long long nt_u64;
@@ -662,51 +665,88 @@ NT_FN double nt_warp_sum(double x) {
 }
 
 /*
- * Reduces `channels` per-thread accumulators to one record per block, then the
- * last block to finish (atomic ticket, no waiting) sums the block records in
- * block order and writes (or adds) the grid total.  `scratch` must hold
- * channels * (blockDim.x / 32) doubles of shared memory.
- *   partials: gridDim.x * channels doubles (global)
- *   ticket:   one counter, zero on entry, left zero on exit
- *   out:      channels doubles; written when accumulate == 0, else added to
+ * Per-path accumulation of the replay kernels, exact and independent of how
+ * the path range is split.  A warp replays one tile of 32 consecutive paths
+ * of the launch (lanes past the end contribute 0).  For each channel the
+ * lanes' values are summed by a fixed xor butterfly (nt_warp_allsum), which
+ * leaves the same bits in every lane (each step adds the same two values in
+ * either order); lane k % 32 keeps channel k's tile sum in a register until
+ * the tile is done, then adds it to the block's exact words (nt_exact.cuh)
+ * in shared memory, or straight to the launch's words in global memory when
+ * the channels' words do not fit in shared memory (nt_tile_xadd).  A tile's
+ * sum depends on its 32 paths alone and the words add exactly, so the
+ * launch total is the same whatever grid, chunking or number of GPUs
+ * produced it, as long as tiles start at the same paths.  Every lane of the
+ * warp must call nt_warp_allsum at the same point.
  */
-NT_FN void nt_grid_reduce(const double* acc, int channels, double* scratch, double* partials,
-                          unsigned int* ticket, double* out, int accumulate) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int warps = blockDim.x >> 5;
-  for (int c = 0; c < channels; ++c) {
-    double v = nt_warp_sum(acc[c]);
-    if (lane == 0) scratch[c * warps + warp] = v;
+NT_FN double nt_warp_allsum(double x) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+
+/* Adds this lane's tile sums (channel lane + 32 r in ws[r]) to the words. */
+NT_FN void nt_tile_xadd(nt_i64* words, const double* ws, int nws, int channels) {
+  const int lane = (int)(threadIdx.x & 31);
+#pragma unroll
+  for (int r = 0; r < nws; ++r) {
+    const int k = lane + 32 * r;
+    if (k < channels) nt_exact_add_atomic(words + (nt_u64)k * NT_XWORDS, ws[r]);
   }
+}
+
+/*
+ * Block -> launch: when `fold` is set, adds the block's exact words (shared,
+ * `channels` records of NT_XWORDS) to the launch's words `glim` (global, zero
+ * on entry); a kernel whose channels' words do not fit in shared memory adds
+ * its tile sums to glim directly and passes fold = 0.  Then the last block to
+ * finish (atomic ticket, no waiting) either writes the correctly rounded sums
+ * to out[0..channels) (accumulate == 0) or adds the launch's words to the
+ * accumulator words `acc` and carries them (accumulate != 0).  It leaves glim
+ * and the ticket zero for the next launch.
+ */
+NT_FN void nt_xgrid_finish(const nt_i64* blk, int fold, int channels, nt_i64* glim, unsigned int* ticket,
+                           double* out, nt_i64* acc, int accumulate) {
   __syncthreads();
-  for (int c = threadIdx.x; c < channels; c += blockDim.x) {
-    double s = 0.0;
-    for (int w = 0; w < warps; ++w) s += scratch[c * warps + w];
-    partials[(nt_u64)blockIdx.x * channels + c] = s;
-  }
+  const int words = channels * NT_XWORDS;
+  if (fold)
+    for (int i = threadIdx.x; i < words; i += blockDim.x) {
+      const nt_i64 v = blk[i];
+      if (v) atomicAdd((nt_x64*)&glim[i], (nt_x64)v);
+    }
   __shared__ unsigned int last;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) last = (atomicAdd(ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
   __syncthreads();
-  if (last) {
-    __threadfence();
-    for (int c = threadIdx.x; c < channels; c += blockDim.x) {
-      double s = 0.0;
-      for (unsigned int b = 0; b < gridDim.x; ++b) s += __ldcg(&partials[(nt_u64)b * channels + c]);
-      out[c] = accumulate ? out[c] + s : s;
+  if (!last) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+    nt_i64* g = glim + (nt_u64)c * NT_XWORDS;
+    if (accumulate) {
+      nt_i64* a = acc + (nt_u64)c * NT_XWORDS;
+      NT_XLOOP
+      for (int i = 0; i < NT_XWORDS; ++i) {
+        a[i] += __ldcg(&g[i]);
+        g[i] = 0;
+      }
+      nt_exact_normalize(a);
+    } else {
+      out[c] = nt_exact_round_inplace(g);
+      NT_XLOOP
+      for (int i = 0; i < NT_XWORDS; ++i) g[i] = 0;
     }
-    if (threadIdx.x == 0) *ticket = 0u;
   }
+  if (threadIdx.x == 0) *ticket = 0u;
 }
 
-/* nt_grid_reduce for per-thread compensated sums kept in a block tile (the
- * multi-market kernel, whose channel count is a launch argument): channel k
- * of this thread is col[2k * stride] + col[(2k + 1) * stride].  Channels pass
- * through the block `chunk` at a time (scratch holds chunk * warps doubles);
- * the block records and the last-block sum are as in nt_grid_reduce, so the
- * result is the same block-order sum. */
+/* The multi-market kernel's reduction, whose channel count is a launch
+ * argument: per-thread compensated sums kept in a block tile, channel k of
+ * this thread being col[2k * stride] + col[(2k + 1) * stride].  Channels pass
+ * through the block `chunk` at a time (scratch holds chunk * warps doubles):
+ * warp shuffle, then one record per block; the last block to finish (atomic
+ * ticket, no waiting) sums the block records in block order and writes (or,
+ * when accumulate != 0, adds to) out. */
 NT_FN void nt_grid_reduce_cols(const double* col, int stride, int channels, int chunk, double* scratch,
                                double* partials, unsigned int* ticket, double* out, int accumulate) {
   const int lane = threadIdx.x & 31;

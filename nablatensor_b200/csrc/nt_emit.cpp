@@ -61,19 +61,19 @@ std::string lit(double x, bool f32) {
 class Emitter {
  public:
   Emitter(const Tape& t, const Plan& p, const EmitConfig& cfg)
-      : t_(t), p_(p), lp_(p.loop), cfg_(cfg),
-        // Shared-memory accumulators only while they fit in 32 KB per block
-        // (a tape with hundreds of inputs keeps them in registers instead).
-        acc_smem_(cfg.acc_smem && 2ll * (2 + t.n_in()) * t.n_out() * cfg.block * 8 <= 32 * 1024) {}
+      : t_(t), p_(p), lp_(p.loop), cfg_(cfg) {}
 
   std::string run();
 
  private:
+  // The block's exact words live in shared memory while they take at most
+  // 24 KB (44 channels of 69 words); beyond that the kernel adds its tile
+  // sums to the launch's words in global memory.
+  bool xshared() const { return (int64_t)channels() * kXWords * 8 <= 24 * 1024; }
   const Tape& t_;
   const Plan& p_;
   const Loop& lp_;
   const EmitConfig& cfg_;
-  const bool acc_smem_;
   Out o_;
   // Adjoint registers that still hold their initial zero at this point of the
   // emitted straight-line code.  In fp64 the first contribution to one is
@@ -522,15 +522,20 @@ void Emitter::emit_reverse_for_output(int o) {
   o_.close();
 }
 
-// Per-thread accumulation: compensated (TwoSum) on the device; a plain
-// running sum in the host target, which reproduces AadTotals.add exactly.
+// Per-path accumulation.  The replay kernel sums each warp tile of 32 paths
+// with a fixed butterfly (lane k % 32 keeps channel k's tile sum) and adds the
+// tile sums exactly at the end of the tile (nt_tile_xadd), so its totals do
+// not depend on the grid, the chunking or the GPU count; the multi-market
+// kernel keeps compensated (TwoSum) per-thread sums; the host target keeps a
+// plain running sum, which reproduces AadTotals.add exactly.
 void Emitter::acc_line(int32_t k, const std::string& x) {
   const std::string K = std::to_string(k);
   if (cfg_.target == 1 && cfg_.markets) o_.line("nt_acc[nt_m * NT_CH + " + K + "] += " + x + ";");
   else if (cfg_.target == 1) o_.line("nt_acc[" + K + "] += " + x + ";");
   else if (cfg_.markets) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
-  else if (acc_smem_) o_.line("nt_two_sum(&NT_ACC(" + K + "), &NT_CMP(" + K + "), " + x + ");");
-  else o_.line("nt_two_sum(&nt_acc[" + K + "], &nt_cmp[" + K + "], " + x + ");");
+  else
+    o_.line("{ const double nt_s = nt_warp_allsum(nt_live ? " + x + " : 0.0); if (nt_lane == " + std::to_string(k % 32) +
+            "u) nt_ws[" + std::to_string(k / 32) + "] = nt_s; }");
 }
 
 // True when no gathered node depends on a draw: then every path of a launch
@@ -738,6 +743,7 @@ std::string Emitter::run() {
   o_.line("#include \"nt_device_rt.cuh\"");
   o_.line(std::string("typedef ") + (cfg_.f32 ? "float" : "double") + " real;");
   o_.line("#define NT_CH " + std::to_string(channels()));
+  o_.line("#define NT_WS " + std::to_string((channels() + 31) / 32));
   o_.line("#define NT_NIN " + std::to_string(std::max(1, t_.n_in())));
   const int32_t ntape = lp_.present ? lp_.n_tape : 0;
   o_.line("#define NT_NTAPE " + std::to_string(std::max(1, ntape)));
@@ -831,12 +837,12 @@ std::string Emitter::run() {
   } else {
     o_.line("extern \"C\" __global__ void " + bounds + " nt_replay_kernel(");
     o_.line("    const double* __restrict__ inputs, nt_u64 n_paths, nt_u64 path_offset, nt_u64 seed,");
-    o_.line("    double* __restrict__ partials, unsigned int* __restrict__ ticket, double* __restrict__ out,");
-    o_.line("    int accumulate, real* __restrict__ nt_gck, real* __restrict__ nt_tape) {");
+    o_.line("    nt_i64* __restrict__ glim, unsigned int* __restrict__ ticket, double* __restrict__ out,");
+    o_.line("    nt_i64* __restrict__ acc, int accumulate, real* __restrict__ nt_gck, real* __restrict__ nt_tape) {");
   }
   ++o_.ind;
   if (!cfg_.global_ckpt) o_.line("extern __shared__ real nt_ck[];");
-  o_.line("__shared__ double nt_red[NT_CH * (NT_BLOCK / 32)];");
+  if (mk) o_.line("__shared__ double nt_red[NT_CH * (NT_BLOCK / 32)];");
   o_.line("const nt_u64 nt_gtid = (nt_u64)blockIdx.x * NT_BLOCK + threadIdx.x;");
   o_.line("const nt_u64 nt_gthreads = (nt_u64)gridDim.x * NT_BLOCK;");
   o_.line("(void)nt_gck; (void)nt_gthreads; (void)nt_tape;");
@@ -859,25 +865,33 @@ std::string Emitter::run() {
     o_.line("#define NT_CMP(k) nt_gacc_b[(nt_u64)(2 * (nt_m * NT_CH + (k)) + 1) * NT_BLOCK]");
   } else {
     load_inputs("");
-    if (acc_smem_) {
-      // Compensated accumulators live in shared memory (one column per thread):
-      // they are touched once per scenario, so registers are better spent on
-      // the segment buffer and occupancy.
-      o_.line("__shared__ double nt_accs[2 * NT_CH * NT_BLOCK];");
-      o_.line("#define NT_ACC(k) nt_accs[(2 * (k)) * NT_BLOCK + threadIdx.x]");
-      o_.line("#define NT_CMP(k) nt_accs[(2 * (k) + 1) * NT_BLOCK + threadIdx.x]");
-      o_.line("for (int c = 0; c < NT_CH; ++c) { NT_ACC(c) = 0.0; NT_CMP(c) = 0.0; }");
+    if (xshared()) {
+      // The block's exact words (nt_exact.cuh), one record per channel.
+      o_.line("__shared__ nt_i64 nt_xblk[NT_CH * NT_XWORDS];");
+      o_.line("for (int i = threadIdx.x; i < NT_CH * NT_XWORDS; i += NT_BLOCK) nt_xblk[i] = 0;");
     } else {
-      o_.line("double nt_acc[NT_CH], nt_cmp[NT_CH];");
-      o_.line("#pragma unroll");
-      o_.line("for (int c = 0; c < NT_CH; ++c) { nt_acc[c] = 0.0; nt_cmp[c] = 0.0; }");
+      // Too many channels for shared memory: tile sums go straight to the
+      // launch's words.
+      o_.line("nt_i64* const nt_xblk = glim;");
     }
   }
-  o_.line("nt_math_tables_load();");
+  o_.line("nt_math_tables_load();");  // ends with __syncthreads()
   if (gv_shared_) emit_shared_gather();
-  o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
-  o_.line("const nt_u64 path = p + path_offset;");
-  o_.line("const unsigned nt_lanes = __activemask();");
+  if (mk) {
+    o_.open("for (nt_u64 p = nt_gtid; p < n_paths; p += nt_gthreads) {");
+    o_.line("const nt_u64 path = p + path_offset;");
+    o_.line("const unsigned nt_lanes = __activemask();");
+  } else {
+    // Warp tiles: the warp's lanes replay 32 consecutive paths of the launch,
+    // the tile starting at a multiple of 32.  Lanes past the end replay the
+    // tile's first path again (so they vote as it does) and contribute 0.
+    o_.line("const unsigned nt_lane = threadIdx.x & 31u;");
+    o_.open("for (nt_u64 nt_pw = nt_gtid - nt_lane; nt_pw < n_paths; nt_pw += nt_gthreads) {");
+    o_.line("const bool nt_live = nt_pw + nt_lane < n_paths;");
+    o_.line("const nt_u64 path = (nt_live ? nt_pw + nt_lane : nt_pw) + path_offset;");
+    o_.line("const unsigned nt_lanes = 0xffffffffu;");
+    o_.line("double nt_ws[NT_WS];  // this lane's tile sums: channel nt_lane + 32 r in nt_ws[r]");
+  }
   o_.line("(void)nt_lanes;");
   if (mk) {
     o_.open("for (int nt_m = 0; nt_m < n_states; ++nt_m) {");
@@ -886,21 +900,15 @@ std::string Emitter::run() {
     o_.close();
   } else {
     emit_scenario();
+    o_.line("nt_tile_xadd(nt_xblk, nt_ws, NT_WS, NT_CH);");
   }
   o_.close();
   if (mk) {
     o_.line("nt_grid_reduce_cols(nt_gacc_b, NT_BLOCK, n_states * NT_CH, NT_CH, nt_red, partials, ticket, out, "
             "accumulate);");
   } else {
-    if (acc_smem_) {
-      o_.line("double nt_acc[NT_CH];");
-      o_.line("#pragma unroll");
-      o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] = NT_ACC(c) + NT_CMP(c);");
-    } else {
-      o_.line("#pragma unroll");
-      o_.line("for (int c = 0; c < NT_CH; ++c) nt_acc[c] += nt_cmp[c];");
-    }
-    o_.line("nt_grid_reduce(nt_acc, NT_CH, nt_red, partials, ticket, out, accumulate);");
+    o_.line(std::string("nt_xgrid_finish(nt_xblk, ") + (xshared() ? "1" : "0") +
+            ", NT_CH, glim, ticket, out, acc, accumulate);");
   }
   o_.close();
   return o_.s;

@@ -4,15 +4,21 @@
 // The reference's device executable (nablatensor-core/.../DeviceAadExecutable.java:140-221)
 // launched 256-thread blocks over min(ceil(paths/256), 4096) blocks, copied
 // one partial record per block to the host and summed there.  Here:
-//   - one persistent grid of (SMs x resident blocks) walks the path range;
-//   - the grid reduction finishes on the device (atomic ticket, no spin) and
-//     the host reads n_out*(2+n_in) doubles;
-//   - long runs accumulate on the device across dispatches;
-//   - several GPUs split the range into contiguous shards and all-reduce the
-//     sums vector once (NCCL over NVLink/NVSwitch).
+//   - one persistent grid of (SMs x resident blocks) walks the path range in
+//     warp tiles of 32 paths;
+//   - every tile's sums are added exactly into fixed-point words
+//     (nt_exact.cuh), so the result is the correctly rounded sum of the tile
+//     sums, the same bits for any grid, chunking or number of GPUs;
+//   - the last block rounds the words on the device (atomic ticket, no spin)
+//     and the host reads n_out*(2+n_in) doubles;
+//   - long runs accumulate exact words on the device across dispatches;
+//   - several GPUs split the range into contiguous runs of tiles and
+//     all-reduce the words once (one int64 NCCL all-reduce over
+//     NVLink/NVSwitch).
 #include "nt_exec.hpp"
 
-#include <dlfcn.h>
+#define NT_HOST 1
+#include "nt_exact.cuh"
 
 #include <algorithm>
 #include <chrono>
@@ -20,6 +26,8 @@
 #include <thread>
 
 namespace nt {
+
+static_assert(kXWords == NT_XWORDS, "exact-sum word count");
 
 // ---- driver API through the runtime's entry-point query (no libcuda link) ----
 
@@ -76,74 +84,6 @@ void cu_check(CUresult r, const char* what) {
   const char* name = "?";
   if (driver().getErrorName) driver().getErrorName(r, &name);
   fail(NT_E_CUDA, std::string(what) + ": " + name);
-}
-
-// ---- NCCL through dlopen (the process may already hold torch's copy) ----
-
-struct Nccl {
-  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
-  ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
-  ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
-  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
-  ncclResult_t (*commFinalize)(ncclComm_t) = nullptr;
-  ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
-                            cudaStream_t) = nullptr;
-  const char* (*getErrorString)(ncclResult_t) = nullptr;
-  bool ok = false;
-  std::string err;
-};
-
-Nccl& nccl() {
-  static Nccl n;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
-    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) {
-      n.err = std::string("cannot load libnccl.so.2: ") + dlerror();
-      return;
-    }
-    auto sym = [&](const char* s) { return dlsym(h, s); };
-    n.getUniqueId = (decltype(n.getUniqueId))sym("ncclGetUniqueId");
-    n.commInitRankConfig = (decltype(n.commInitRankConfig))sym("ncclCommInitRankConfig");
-    n.commGetAsyncError = (decltype(n.commGetAsyncError))sym("ncclCommGetAsyncError");
-    n.commAbort = (decltype(n.commAbort))sym("ncclCommAbort");
-    n.commDestroy = (decltype(n.commDestroy))sym("ncclCommDestroy");
-    n.commFinalize = (decltype(n.commFinalize))sym("ncclCommFinalize");
-    n.allReduce = (decltype(n.allReduce))sym("ncclAllReduce");
-    n.getErrorString = (decltype(n.getErrorString))sym("ncclGetErrorString");
-    n.ok = n.getUniqueId && n.commInitRankConfig && n.commGetAsyncError && n.commAbort && n.commDestroy &&
-           n.allReduce && n.getErrorString;
-    if (!n.ok) n.err = "libnccl.so.2 lacks a required symbol";
-  });
-  if (!n.ok) fail(NT_E_NCCL, n.err);
-  return n;
-}
-
-void nccl_check(ncclResult_t r, const char* what) {
-  if (r == ncclSuccess || r == ncclInProgress) return;
-  fail(NT_E_NCCL, std::string(what) + ": " + nccl().getErrorString(r));
-}
-
-// Polls a non-blocking communicator until its pending work is enqueued or the
-// deadline passes; on expiry the communicator is aborted.
-void nccl_wait(ncclComm_t comm, int timeout_ms, const char* what) {
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    ncclResult_t st = ncclSuccess;
-    nccl().commGetAsyncError(comm, &st);
-    if (st == ncclSuccess) return;
-    if (st != ncclInProgress) {
-      nccl().commAbort(comm);
-      fail(NT_E_NCCL, std::string(what) + ": " + nccl().getErrorString(st));
-    }
-    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
-      nccl().commAbort(comm);
-      fail(NT_E_NCCL, std::string(what) + ": timed out");
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
-  }
 }
 
 }  // namespace
@@ -275,13 +215,15 @@ void Exec::load(int max_regs) {
   grid = sm_count * per_sm;
   cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
   cuda_check(cudaMalloc(&d_inputs, sizeof(double) * std::max<int32_t>(1, tape.n_in())), "cudaMalloc inputs");
-  cuda_check(cudaMalloc(&d_partials, sizeof(double) * (size_t)grid * channels), "cudaMalloc partials");
+  const size_t words = sizeof(long long) * (size_t)channels * kXWords;
+  cuda_check(cudaMalloc(&d_glim, words), "cudaMalloc exact words");
   cuda_check(cudaMalloc(&d_ticket, sizeof(unsigned int)), "cudaMalloc ticket");
   cuda_check(cudaMalloc(&d_out, sizeof(double) * channels), "cudaMalloc out");
-  cuda_check(cudaMalloc(&d_acc, sizeof(double) * channels), "cudaMalloc accumulator");
-  cuda_check(cudaMalloc(&d_red, sizeof(double) * channels), "cudaMalloc reduced");
+  cuda_check(cudaMalloc(&d_acc, words), "cudaMalloc accumulator");
+  cuda_check(cudaMemset(d_glim, 0, words), "cudaMemset exact words");
   cuda_check(cudaMemset(d_ticket, 0, sizeof(unsigned int)), "cudaMemset ticket");
-  cuda_check(cudaMemset(d_acc, 0, sizeof(double) * channels), "cudaMemset accumulator");
+  cuda_check(cudaMemset(d_acc, 0, words), "cudaMemset accumulator");
+  cuda_check(cudaEventCreateWithFlags(&ev_shard, cudaEventDisableTiming), "cudaEventCreate");
   if (cfg.global_ckpt && ckpt_values(plan) > 0) {
     const size_t bytes = (size_t)ckpt_values(plan) * grid * cfg.block * (cfg.f32 ? 4 : 8);
     cuda_check(cudaMalloc(&d_gck, bytes), "cudaMalloc checkpoints");
@@ -294,6 +236,7 @@ void Exec::load(int max_regs) {
     cuda_check(cudaMalloc(&d_tape, tape_bytes), "cudaMalloc value tape");
   }
   cuda_check(cudaMallocHost(&h_stage, sizeof(double) * (tape.n_in() + 2 * channels + 2)), "cudaMallocHost");
+  cuda_check(cudaMallocHost(&h_words, words), "cudaMallocHost");
   compile_seconds = secs + std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   std::memset(&info, 0, sizeof info);
   info.registers = regs;
@@ -325,18 +268,14 @@ void Exec::load(int max_regs) {
 }
 
 Exec::~Exec() {
-  if (comm) {
-    nccl().commDestroy((ncclComm_t)comm);
-    comm = nullptr;
-  }
+  comm.reset();
   if (device >= 0) cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
   cudaFree(d_inputs);
-  cudaFree(d_partials);
+  cudaFree(d_glim);
   cudaFree(d_ticket);
   cudaFree(d_out);
   cudaFree(d_acc);
-  cudaFree(d_red);
   cudaFree(d_gck);
   cudaFree(d_tape);
   cudaFree(d_mk_inputs);
@@ -346,6 +285,8 @@ Exec::~Exec() {
   cudaFree(d_mk_gck);
   cudaFree(d_mk_tape);
   if (h_stage) cudaFreeHost(h_stage);
+  if (h_words) cudaFreeHost(h_words);
+  if (ev_shard) cudaEventDestroy(ev_shard);
   if (stream) cudaStreamDestroy(stream);
   if (module) driver().moduleUnload(module);
   if (mk_module) driver().moduleUnload(mk_module);
@@ -362,14 +303,14 @@ void Exec::upload_inputs_if_dirty() {
   dirty = false;
 }
 
-void Exec::launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, int accumulate) {
+void Exec::launch(uint64_t paths, uint64_t offset, uint64_t seed, int accumulate) {
   if (paths == 0) fail(NT_E_INVALID_ARG, "paths must be positive");
   const uint64_t need = (paths + cfg.block - 1) / cfg.block;
   const unsigned g = (unsigned)std::min<uint64_t>(need, (uint64_t)grid);
   void* gck = d_gck;
   void* tp = d_tape;
   unsigned long long n = paths, off = offset, sd = seed;
-  void* args[] = {&d_inputs, &n, &off, &sd, &d_partials, &d_ticket, &out, &accumulate, &gck, &tp};
+  void* args[] = {&d_inputs, &n, &off, &sd, &d_glim, &d_ticket, &d_out, &d_acc, &accumulate, &gck, &tp};
   cu_check(driver().launchKernel(function, g, 1, 1, (unsigned)cfg.block, 1, 1, (unsigned)dyn_smem,
                                  (CUstream)stream, args, nullptr),
            "cuLaunchKernel");
@@ -381,14 +322,15 @@ unsigned Exec::grid_for(uint64_t paths) const {
   return (unsigned)std::max<uint64_t>(1, std::min<uint64_t>(need, (uint64_t)grid));
 }
 
-void Exec::launch_external(uint64_t paths, uint64_t offset, uint64_t seed, const double* d_in, double* d_out,
-                           unsigned int* ticket, double* partials, cudaStream_t s, unsigned grid_blocks) {
+void Exec::launch_external(uint64_t paths, uint64_t offset, uint64_t seed, const double* d_in, double* d_sums,
+                           unsigned int* ticket, long long* glim, cudaStream_t s, unsigned grid_blocks) {
   void* gck = nullptr;
   void* tp = nullptr;
   const double* in = d_in;
+  long long* no_acc = nullptr;
   int accumulate = 0;
   unsigned long long n = paths, off = offset, sd = seed;
-  void* args[] = {&in, &n, &off, &sd, &partials, &ticket, &d_out, &accumulate, &gck, &tp};
+  void* args[] = {&in, &n, &off, &sd, &glim, &ticket, &d_sums, &no_acc, &accumulate, &gck, &tp};
   cu_check(driver().launchKernel(function, grid_blocks, 1, 1, (unsigned)cfg.block, 1, 1, (unsigned)dyn_smem,
                                  (CUstream)s, args, nullptr),
            "cuLaunchKernel");
@@ -398,7 +340,7 @@ void Exec::replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, 
   const auto t0 = std::chrono::steady_clock::now();
   bind();
   upload_inputs_if_dirty();
-  launch(paths, offset, seed, d_out, 0);
+  launch(paths, offset, seed, 0);
   double* h_out = h_stage + tape.n_in();
   cuda_check(cudaMemcpyAsync(h_out, d_out, sizeof(double) * channels, cudaMemcpyDeviceToHost, stream), "read sums");
   cuda_check(cudaStreamSynchronize(stream), "replay");
@@ -496,26 +438,34 @@ void Exec::markets(int32_t n_states, const double* h_inputs, uint64_t paths, uin
 void Exec::accumulate(uint64_t paths, uint64_t offset, uint64_t seed) {
   bind();
   upload_inputs_if_dirty();
-  launch(paths, offset, seed, d_acc, 1);
+  launch(paths, offset, seed, 1);
 }
 
+// The accumulator holds exact words; the host rounds each channel's sum.
 void Exec::read_accumulator(double* sums, bool reset) {
   bind();
-  double* h_out = h_stage + tape.n_in();
-  cuda_check(cudaMemcpyAsync(h_out, d_acc, sizeof(double) * channels, cudaMemcpyDeviceToHost, stream), "read sums");
-  if (reset) cuda_check(cudaMemsetAsync(d_acc, 0, sizeof(double) * channels, stream), "reset accumulator");
+  const size_t words = sizeof(long long) * (size_t)channels * kXWords;
+  cuda_check(cudaMemcpyAsync(h_words, d_acc, words, cudaMemcpyDeviceToHost, stream), "read sums");
+  if (reset) cuda_check(cudaMemsetAsync(d_acc, 0, words, stream), "reset accumulator");
   cuda_check(cudaStreamSynchronize(stream), "read accumulator");
-  std::memcpy(sums, h_out, sizeof(double) * channels);
+  for (int32_t c = 0; c < channels; ++c) sums[c] = nt_exact_to_double(h_words + (size_t)c * kXWords);
 }
 
 // ---- sharding + all-reduce ------------------------------------------------------
 
+// Shards are whole warp tiles: rank r takes a contiguous run of the
+// ceil(total / 32) tiles of the range (the first ones one tile more when they
+// do not divide evenly), so a tile never straddles two ranks and every rank's
+// tiles hold the same paths as in a single-GPU replay.
 void shard_range(uint64_t total, uint64_t offset, int32_t nranks, int32_t rank, uint64_t* from, uint64_t* count) {
   if (nranks < 1 || rank < 0 || rank >= nranks) fail(NT_E_INVALID_ARG, "bad rank / world size");
   const uint64_t r = (uint64_t)rank, n = (uint64_t)nranks;
-  const uint64_t base = total / n, extra = total % n;
-  *from = offset + r * base + std::min(r, extra);
-  *count = base + (r < extra ? 1 : 0);
+  const uint64_t tiles = total / kTile + (total % kTile ? 1 : 0);
+  const uint64_t base = tiles / n, extra = tiles % n;
+  const uint64_t t0 = r * base + std::min(r, extra), nt = base + (r < extra ? 1 : 0);
+  const uint64_t lo = std::min(total, t0 * kTile), hi = std::min(total, (t0 + nt) * kTile);
+  *from = offset + lo;
+  *count = hi - lo;
 }
 
 void Exec::shard(uint64_t total, uint64_t offset, uint64_t* from, uint64_t* count) const {
@@ -524,50 +474,48 @@ void Exec::shard(uint64_t total, uint64_t offset, uint64_t* from, uint64_t* coun
 
 void Exec::sharded_enqueue(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk) {
   if (total == 0) fail(NT_E_INVALID_ARG, "paths must be positive");
+  if (nranks > 1 && !comm) fail(NT_E_STATE, "executable is not attached to a communicator");
   bind();
   upload_inputs_if_dirty();
   uint64_t from = 0, count = 0;
   shard(total, offset, &from, &count);
-  cuda_check(cudaMemsetAsync(d_acc, 0, sizeof(double) * channels, stream), "reset accumulator");
-  const uint64_t step = chunk > 0 ? chunk : count;
+  cuda_check(cudaMemsetAsync(d_acc, 0, sizeof(long long) * (size_t)channels * kXWords, stream), "reset accumulator");
+  // Chunks are whole tiles too, so the chunking changes no tile.
+  const uint64_t step = chunk > 0 ? std::max<uint64_t>(kTile, chunk - chunk % kTile) : count;
   for (uint64_t done = 0; done < count; done += step) {
     const uint64_t k = std::min(step, count - done);
-    launch(k, from + done, seed, d_acc, 1);
+    launch(k, from + done, seed, 1);
   }
   if (nranks > 1) {
-    if (!comm) fail(NT_E_STATE, "executable is not attached to a communicator");
-    nccl_check(nccl().allReduce(d_acc, d_acc, (size_t)channels, ncclFloat64, ncclSum, (ncclComm_t)comm, stream),
-               "ncclAllReduce");
-    nccl_wait((ncclComm_t)comm, dist_timeout_ms, "ncclAllReduce");
+    // The exact words of every rank add up to the words of the whole range:
+    // one int64 all-reduce, and the sums are the same bits on any number of
+    // GPUs.
+    cuda_check(cudaEventRecord(ev_shard, stream), "cudaEventRecord");
+    comm->allreduce_i64(d_acc, (size_t)channels * kXWords, (void*)stream);
   }
 }
 
 void Exec::sharded(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk, double* sums, double* seconds) {
   const auto t0 = std::chrono::steady_clock::now();
-  sharded_enqueue(total, offset, seed, chunk);
-  // Bounded wait: a peer that never joins the all-reduce ends this call with
-  // an error instead of a hang.
-  if (nranks > 1) {
-    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(dist_timeout_ms) +
-                          std::chrono::seconds(600);
-    for (;;) {
-      cudaError_t q = cudaStreamQuery(stream);
-      if (q == cudaSuccess) break;
-      if (q != cudaErrorNotReady) cuda_check(q, "sharded replay");
-      ncclResult_t st = ncclSuccess;
-      nccl().commGetAsyncError((ncclComm_t)comm, &st);
-      if (st != ncclSuccess && st != ncclInProgress) {
-        nccl().commAbort((ncclComm_t)comm);
-        comm = nullptr;
-        fail(NT_E_NCCL, std::string("all-reduce failed: ") + nccl().getErrorString(st));
-      }
-      if (std::chrono::steady_clock::now() > deadline) {
-        nccl().commAbort((ncclComm_t)comm);
-        comm = nullptr;
-        fail(NT_E_NCCL, "all-reduce timed out");
-      }
-      std::this_thread::sleep_for(std::chrono::microseconds(20));
+  try {
+    sharded_enqueue(total, offset, seed, chunk);
+    if (nranks > 1) {
+      // Bounded wait: once this rank's shard has finished, a peer that never
+      // joins the all-reduce ends the call with NT_E_NCCL within the
+      // communicator's timeout instead of a hang.
+      comm->wait([&] {
+        const cudaError_t q = cudaStreamQuery(stream);
+        if (q == cudaSuccess) return Comm::Progress::Done;
+        if (q != cudaErrorNotReady) cuda_check(q, "sharded replay");
+        const cudaError_t e = cudaEventQuery(ev_shard);
+        if (e == cudaSuccess) return Comm::Progress::Collective;
+        if (e != cudaErrorNotReady) cuda_check(e, "sharded replay");
+        return Comm::Progress::Computing;
+      });
     }
+  } catch (...) {
+    if (comm && comm->aborted()) comm.reset();
+    throw;
   }
   read_accumulator(sums, true);
   if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
@@ -576,42 +524,22 @@ void Exec::sharded(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chun
 void Exec::attach(int32_t n, int32_t r, const uint8_t id[128], int32_t timeout_ms) {
   if (n < 1 || r < 0 || r >= n) fail(NT_E_INVALID_ARG, "bad rank / world size");
   if (comm) fail(NT_E_STATE, "already attached");
+  if (n > 1) {
+    bind();
+    comm = std::make_unique<Comm>(n, r, id, timeout_ms);
+  }
   nranks = n;
   rank = r;
-  dist_timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
-  if (n == 1) return;
-  bind();
-  ncclUniqueId uid;
-  static_assert(sizeof(uid.internal) == 128, "NCCL unique id is 128 bytes");
-  std::memcpy(uid.internal, id, 128);
-  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
-  config.blocking = 0;
-  ncclComm_t c = nullptr;
-  nccl_check(nccl().commInitRankConfig(&c, n, uid, r, &config), "ncclCommInitRankConfig");
-  comm = c;
-  try {
-    nccl_wait(c, dist_timeout_ms, "ncclCommInitRank");
-  } catch (...) {
-    comm = nullptr;
-    throw;
-  }
 }
 
 void Exec::detach() {
   if (comm) {
     bind();
     cudaStreamSynchronize(stream);
-    nccl().commDestroy((ncclComm_t)comm);
-    comm = nullptr;
+    comm.reset();
   }
   nranks = 1;
   rank = 0;
-}
-
-void dist_unique_id(uint8_t out[128]) {
-  ncclUniqueId uid;
-  nccl_check(nccl().getUniqueId(&uid), "ncclGetUniqueId");
-  std::memcpy(out, uid.internal, 128);
 }
 
 }  // namespace nt

@@ -3,17 +3,16 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
-#include <nccl.h>
 
 #include <memory>
 #include <mutex>
 
+#include "nt_dist.hpp"
 #include "nt_internal.hpp"
 
 namespace nt {
 
 void cuda_check(cudaError_t e, const char* what);
-void dist_unique_id(uint8_t out[128]);
 void shard_range(uint64_t total, uint64_t offset, int32_t nranks, int32_t rank, uint64_t* from, uint64_t* count);
 size_t noalloc_scratch_bytes();
 
@@ -34,14 +33,15 @@ struct Exec {
   int sm_count = 0, blocks_per_sm = 0, grid = 0, dyn_smem = 0;
   int32_t channels = 0;
   double* d_inputs = nullptr;
-  double* d_partials = nullptr;
+  long long* d_glim = nullptr;  // a launch's exact words, channels x kXWords (left zero by every launch)
   unsigned int* d_ticket = nullptr;
-  double* d_out = nullptr;
-  double* d_acc = nullptr;
-  double* d_red = nullptr;
+  double* d_out = nullptr;      // a launch's rounded sums
+  long long* d_acc = nullptr;   // the device accumulator: exact words, channels x kXWords
   void* d_gck = nullptr;
   void* d_tape = nullptr;
-  double* h_stage = nullptr;  // pinned: inputs, then sums
+  double* h_stage = nullptr;    // pinned: inputs, then sums
+  long long* h_words = nullptr; // pinned: the accumulator's words on their way to the host
+  cudaEvent_t ev_shard = nullptr;  // recorded once this rank's shard is enqueued, before the all-reduce
   std::vector<double> inputs;
   bool dirty = true;
   double compile_seconds = 0.0;
@@ -60,8 +60,8 @@ struct Exec {
   void* d_mk_gck = nullptr;
   void* d_mk_tape = nullptr;
   // multi-GPU
-  void* comm = nullptr;
-  int32_t nranks = 1, rank = 0, dist_timeout_ms = 60000;
+  std::unique_ptr<Comm> comm;
+  int32_t nranks = 1, rank = 0;
 
   static Exec* create(const nt_tape* tape, const nt_options* opt);
   ~Exec();
@@ -69,11 +69,14 @@ struct Exec {
   void bind() const;
   void load(int max_regs);
   void upload_inputs_if_dirty();
-  void launch(uint64_t paths, uint64_t offset, uint64_t seed, double* out, int accumulate);
+  // accumulate == 0: the rounded sums go to d_out; else the exact words are
+  // added to d_acc.
+  void launch(uint64_t paths, uint64_t offset, uint64_t seed, int accumulate);
   // Launch with caller-provided device pointers on a caller stream (no
-  // executable-owned buffers); `grid` blocks.
+  // executable-owned buffers); `grid` blocks, the launch's exact words in
+  // `glim` (zero on entry, left zero).
   void launch_external(uint64_t paths, uint64_t offset, uint64_t seed, const double* d_inputs, double* d_out,
-                       unsigned int* ticket, double* partials, cudaStream_t s, unsigned grid_blocks);
+                       unsigned int* ticket, long long* glim, cudaStream_t s, unsigned grid_blocks);
   unsigned grid_for(uint64_t paths) const;
   void replay(uint64_t paths, uint64_t offset, uint64_t seed, double* sums, double* seconds);
   void accumulate(uint64_t paths, uint64_t offset, uint64_t seed);

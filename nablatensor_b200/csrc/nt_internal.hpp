@@ -10,6 +10,14 @@
 
 namespace nt {
 
+// Words of one channel's exact sum (NT_XWORDS of nt_exact.cuh; checked
+// against it where both are visible).
+constexpr int kXWords = 69;
+// Paths of one warp tile: launches and shards start on multiples of it
+// (relative to the start of the whole range), so every tile holds the same
+// paths however the range is split.
+constexpr uint64_t kTile = 32;
+
 // An error that crosses no ABI: the C entry points turn it into a status code
 // and a thread-local message.
 struct Error : std::runtime_error {
@@ -121,7 +129,6 @@ struct EmitConfig {
   bool global_ckpt = false;
   bool wide32 = false;     // fp32: transcendentals + Box-Muller in fp64, narrowed
   bool fmad = true;        // allow multiply-add contraction
-  bool acc_smem = true;    // compensated accumulators in shared memory
   bool tape = true;        // expensive loop values go to a per-thread tape instead of being recomputed
   bool tape_all = true;    // tape draws and transcendentals (else draws only)
   bool tape_every_exp = false;  // tape_all: also the exps of draws and invariants alone
@@ -159,6 +166,7 @@ int32_t ckpt_values(const Plan& p);
 
 extern const char* kDeviceRuntimeSource;  // nt_device_rt.cuh, embedded at build time
 extern const char* kMathTablesSource;     // nt_math_tables.cuh, embedded at build time
+extern const char* kExactSource;          // nt_exact.cuh, embedded at build time
 
 // Frozen flop weights of the fp64 transcendentals {exp, log, sqrt, sincos}
 // (nt_flops.cpp), used for the algorithmic flop count of a tape.

@@ -73,6 +73,7 @@ std::vector<char> nvrtc_compile(const std::string& source, const std::string& ar
   };
   if (max_regs > 0) opts.push_back("--maxrregcount=" + std::to_string(max_regs));
   std::string key_text = source + "\x01" + kDeviceRuntimeSource + "\x01" + kMathTablesSource + "\x01" +
+                         kExactSource + "\x01" +
                          std::to_string(major) + "." + std::to_string(minor);
   for (auto& o : opts) key_text += "\x02" + o;
   const uint64_t key = fnv1a(key_text);
@@ -98,9 +99,9 @@ std::vector<char> nvrtc_compile(const std::string& source, const std::string& ar
   }
   const auto t0 = std::chrono::steady_clock::now();
   nvrtcProgram prog;
-  const char* hdr_src[] = {kDeviceRuntimeSource, kMathTablesSource};
-  const char* hdr_name[] = {"nt_device_rt.cuh", "nt_math_tables.cuh"};
-  check(nvrtcCreateProgram(&prog, source.c_str(), "nt_replay.cu", 2, hdr_src, hdr_name), "nvrtcCreateProgram");
+  const char* hdr_src[] = {kDeviceRuntimeSource, kMathTablesSource, kExactSource};
+  const char* hdr_name[] = {"nt_device_rt.cuh", "nt_math_tables.cuh", "nt_exact.cuh"};
+  check(nvrtcCreateProgram(&prog, source.c_str(), "nt_replay.cu", 3, hdr_src, hdr_name), "nvrtcCreateProgram");
   std::vector<const char*> copts;
   for (auto& o : opts) copts.push_back(o.c_str());
   nvrtcResult rc = nvrtcCompileProgram(prog, (int)copts.size(), copts.data());

@@ -347,7 +347,6 @@ EmitConfig config_from(const nt_options* opt, int32_t target) {
   cfg.fwd_unroll = opt->fwd_unroll;
   if (opt->rev_unroll < 0 || opt->rev_unroll > 8) fail(NT_E_INVALID_ARG, "rev_unroll must be in [0, 8]");
   cfg.rev_unroll = std::max(1, opt->rev_unroll);
-  cfg.acc_smem = (opt->flags & NT_FLAG_ACC_REGS) == 0;
   cfg.tape = (opt->flags & NT_FLAG_RECOMPUTE_ALL) == 0;
   cfg.tape_all = (opt->flags & NT_FLAG_TAPE_DRAWS) == 0;
   cfg.tape_every_exp = (opt->flags & NT_FLAG_TAPE_ALL) != 0;

@@ -331,7 +331,9 @@ class B200AadExecutable(AadExecutable):
 
     def replaySafe(self, total_paths: int, seed: int) -> AadResult:
         """Chunked replay (AbstractAadExecutable.java:101-121); the chunk sums
-        accumulate on the device and are read back once."""
+        accumulate on the device, exactly, and are read back once: the result
+        has the same bits as replay(total_paths, 0, seed), whatever the chunk
+        sizes the time budget picked."""
         if total_paths <= 0:
             raise ValueError("paths must be positive")
         if self._pps <= 0.0:
@@ -369,9 +371,12 @@ class B200AadExecutable(AadExecutable):
         self._pps = sample if self._pps <= 0.0 else 0.5 * (self._pps + sample)
 
     def _budgeted_chunk(self) -> int:
+        """Paths per dispatch for the time budget: a whole number of 32-path
+        warp tiles, so the chunked sums are the bits of one dispatch over the
+        whole range."""
         if self._pps <= 0.0:
             return self.PROBE_PATHS
-        return max(self.MIN_CHUNK_PATHS, int(self._pps * self._max_chunk_seconds))
+        return max(self.MIN_CHUNK_PATHS, int(self._pps * self._max_chunk_seconds) // 32 * 32)
 
     # ---- multi-GPU (scenario-range sharding + one NCCL all-reduce) ----
     def distAttach(self, nranks: int, rank: int, unique_id: bytes, timeout_ms: int = 60000) -> None:
@@ -381,13 +386,22 @@ class B200AadExecutable(AadExecutable):
     def distDetach(self) -> None:
         _lib.check(_lib.lib().nt_dist_detach(self._handle()))
 
-    def replaySharded(self, total_paths: int, path_offset: int, seed: int, chunk_paths: int = 0) -> AadResult:
+    def replaySharded_sums(self, total_paths: int, path_offset: int, seed: int, chunk_paths: int = 0):
+        if total_paths <= 0:
+            raise ValueError("paths must be positive")
         sums = np.zeros(self._channels, dtype=np.float64)
         secs = ctypes.c_double(0.0)
         _lib.check(_lib.lib().nt_replay_sharded(self._handle(), total_paths, path_offset & (2**64 - 1),
                                                 seed & (2**64 - 1), chunk_paths, _lib.ptr(sums, ctypes.c_double),
                                                 ctypes.byref(secs)))
-        return AadResult.from_sums(sums, self._tape, total_paths, secs.value)
+        return sums, secs.value
+
+    def replaySharded(self, total_paths: int, path_offset: int, seed: int, chunk_paths: int = 0) -> AadResult:
+        """This rank's shard of [path_offset, path_offset + total_paths) plus one
+        all-reduce: every rank gets the global result, with the same bits as
+        replay() of the whole range on one GPU."""
+        sums, secs = self.replaySharded_sums(total_paths, path_offset, seed, chunk_paths)
+        return AadResult.from_sums(sums, self._tape, total_paths, secs)
 
     def stream_handle(self) -> int:
         p = ctypes.c_void_p()

@@ -2,15 +2,20 @@
 
 Tolerances (stated by the task and the reference's own tests):
   RNG                uint32 words bit-exact (tests/golden/philox_u32.json)
-  fp64 sums          |gpu - oracle| <= 1e-12 * sum_i |x_i| per channel, where
-                     the oracle sums the same per-path values exactly: the
-                     remaining difference is the device's reduction order
-                     and its libm's last-ulp differences.
+  fp64 sums          |gpu - oracle| <= 1e-12 * |oracle| per channel (plain
+                     relative), and <= 1e-12 * sum_i |x_i|, where the oracle
+                     sums the same per-path values exactly: the remaining
+                     difference is the per-path last-ulp differences of the
+                     transcendentals and the fused multiply-adds.
+  splits of a range  the same bits: the kernel sums 32-path warp tiles exactly,
+                     so grid size, chunking and device accumulation change no
+                     bit of the result.
   loop vs straight   2e-12 (CudaCheckpointParityTest.java:126 fp64 bound)
   fp32 kernel        price within 1e-5 of the fp64 oracle (the benchmark's bound), Greeks
                      within the fp32 oracle's own distance from fp64 plus 1e-5
                      (measured in test_barrier_fp32_against_fp64_oracle).
 """
+import ctypes
 import json
 import os
 
@@ -49,10 +54,15 @@ def _oracle(oracle_mod, tape, inputs, paths, off, seed, f32=False):
     return res.sums, np.array(scale)
 
 
-def _assert_parity(got, want, scale, tol=1e-12):
+def _assert_parity(got, want, scale=None, tol=1e-12, label=""):
+    """Plain relative error per channel (and against sum |x| when given)."""
     err = np.abs(got - want)
-    bound = tol * np.maximum(scale, 1e-300)
-    assert np.all(err <= bound), f"max err/scale {np.max(err / np.maximum(scale, 1e-300)):.3e}"
+    rel = err / np.maximum(np.abs(want), 1e-300)
+    print(f"{label} max relative error vs oracle {rel.max():.3e} (channel {int(np.argmax(rel))})")
+    assert np.all(rel <= tol), f"max relative error {rel.max():.3e} in channel {int(np.argmax(rel))}"
+    if scale is not None:
+        bound = tol * np.maximum(scale, 1e-300)
+        assert np.all(err <= bound), f"max err/scale {np.max(err / np.maximum(scale, 1e-300)):.3e}"
 
 
 def test_philox_words_are_bit_exact(ntlib, oracle_mod):
@@ -212,12 +222,65 @@ def test_mvp_pricing_properties_on_the_gpu(engine):
     assert abs((up - dn) / 2.0 - adj.gradients()[0]) <= 5e-3 and adj.value() > 0.0
 
 
-def test_1m_against_oracle_exact(engine, oracle_mod):
+def _oracle_sums(oracle_mod, tape, inputs, paths, off, seed, f32=False):
+    """The oracle's exactly summed channels on every host thread (no per-path
+    matrix: the full-size configurations have millions of paths)."""
+    return oracle_mod.replay(FlatTape.of(tape), inputs, paths, off, seed, f32=f32, exact=True,
+                             threads=os.cpu_count()).sums
+
+
+def test_config1_full_size_against_oracle(engine, oracle_mod):
+    """Benchmark configuration 1 at its own size: the 252-step Asian, 2,000,000
+    scenarios, seed 42, all seven channels within 1e-12 relative."""
     tape = quant.asian_tape(252)
     with engine.compile(tape, FP64) as ex:
-        got, _ = ex.replay_sums(1_000_000, 0, 42)
-    want, scale = _oracle(oracle_mod, tape, ATM, 1_000_000, 0, 42)
-    _assert_parity(got, want, scale)
+        got, _ = ex.replay_sums(2_000_000, 0, 42)
+    _assert_parity(got, _oracle_sums(oracle_mod, tape, ATM, 2_000_000, 0, 42), label="config 1, 2M")
+
+
+def test_config4_full_size_against_oracle(engine, oracle_mod):
+    """Benchmark configuration 4 at its own size: the 10-asset basket, 10,000,000
+    scenarios, seed 7, all 23 channels (value, value^2, 21 Greeks)."""
+    tape = quant.basket_tape()
+    with engine.compile(tape, FP64) as ex:
+        got, _ = ex.replay_sums(10_000_000, 0, 7)
+    _assert_parity(got, _oracle_sums(oracle_mod, tape, tape.recordedInputs(), 10_000_000, 0, 7),
+                   label="config 4, 10M")
+
+
+def test_config5_full_size_against_oracle(engine, oracle_mod):
+    """Benchmark configuration 5 at its own size: the CVA book, 1,000,000
+    scenarios, seed 11, all 43 channels (CVA, CVA^2, 40 pillars, hazard)."""
+    tape = quant.cva_tape()
+    with engine.compile(tape, FP64) as ex:
+        got, _ = ex.replay_sums(1_000_000, 0, 11)
+    _assert_parity(got, _oracle_sums(oracle_mod, tape, tape.recordedInputs(), 1_000_000, 0, 11),
+                   label="config 5, 1M")
+
+
+def test_config2_full_size_against_both_oracles(engine, oracle_mod):
+    """Benchmark configuration 2 at its own size: the fp32 down-and-in barrier,
+    20,000,000 scenarios, seed 42.  Against the oracle's fp32 mode (the
+    reference's fp32 semantics, ScalarReplay.java:37-51) every channel is
+    within 1e-6.  Against the fp64 oracle the price is within 1e-5 -- the
+    north star's fp32 bound -- but the Greeks are not: the fp32 evaluation of
+    the tape's 1 - survival term loses digits in the reference's own fp32
+    semantics as in this kernel, and rho lands near 3e-5.  The test pins the
+    kernel to where the fp32 oracle itself sits (+1e-6) and prints both."""
+    tape = quant.barrier_tape(252)
+    paths = 20_000_000
+    with engine.compile(tape, FP32) as ex:
+        got, _ = ex.replay_sums(paths, 0, 42)
+    want64 = _oracle_sums(oracle_mod, tape, ATM, paths, 0, 42)
+    want32 = _oracle_sums(oracle_mod, tape, ATM, paths, 0, 42, f32=True)
+    rel32 = np.abs(got - want32) / np.abs(want32)
+    rel_gpu = np.abs(got - want64) / np.abs(want64)
+    rel_orc = np.abs(want32 - want64) / np.abs(want64)
+    print("config 2, 20M: fp32 gpu vs fp32 oracle:", rel32, "\nfp32 gpu vs fp64 oracle:", rel_gpu,
+          "\nfp32 oracle vs fp64 oracle:", rel_orc)
+    assert np.all(rel32 <= 1e-6)
+    assert rel_gpu[0] <= 1e-5
+    assert np.all(rel_gpu <= rel_orc + 1e-6)
 
 
 def test_flop_counts_of_the_asian_tape(engine):
@@ -390,39 +453,77 @@ def test_ladder_over_spot(engine):
     assert delta[2] == pytest.approx(r.gradient("spot"), rel=1e-13)
 
 
-def test_replay_safe_matches_single_dispatch(engine):
+def test_replay_safe_has_the_bits_of_one_dispatch(engine):
+    """replaySafe's time-budgeted chunks accumulate exactly on the device: the
+    result is the single dispatch's, bit for bit."""
     tape = quant.asian_tape(252)
     with engine.compile(tape, FP64) as ex:
         ex.setMaxChunkSeconds(0.002)
         a = ex.replaySafe(3_000_000, 42)
         b = ex.replay(3_000_000, 0, 42)
-    assert a.value() == pytest.approx(b.value(), rel=1e-13)
-    np.testing.assert_allclose(a.gradients(), b.gradients(), rtol=1e-13)
-    assert a.standardError() == pytest.approx(b.standardError(), rel=1e-9)
+    assert a.value() == b.value()
+    np.testing.assert_array_equal(a.gradients(), b.gradients())
+    assert a.standardError() == b.standardError()
+
+
+def _accumulate(ex, pieces, seed):
+    h = ex._handle()
+    sums = np.zeros(ex.info()["channels"], dtype=np.float64)
+    _lib.check(_lib.lib().nt_accumulator_read(h, _lib.ptr(sums, ctypes.c_double), 1))
+    for first, count in pieces:
+        _lib.check(_lib.lib().nt_replay_accumulate(h, count, first, seed))
+    _lib.check(_lib.lib().nt_accumulator_read(h, _lib.ptr(sums, ctypes.c_double), 1))
+    return sums
+
+
+@pytest.mark.parametrize("make,inputs,f32", [
+    (lambda: quant.asian_tape(252), ATM, False),
+    (lambda: quant.barrier_tape(252), ATM, True),
+    (lambda: quant.basket_tape(), None, False),
+    (lambda: quant.cva_tape(), None, False),
+])
+def test_grid_and_chunking_change_no_bit(engine, make, inputs, f32):
+    """The sums of a range are the same bits whatever the persistent grid
+    (one resident block per SM against the default), however the range is
+    split into tile-aligned dispatches accumulated on the device, in any
+    order, and through the single-rank sharded path with a ragged chunk."""
+    tape = make()
+    x = list(tape.recordedInputs()) if inputs is None else inputs
+    opts = FP32 if f32 else FP64
+    total, off, seed = 1_000_003, 0x1_0000_0003, 0x12345678FEDCBA98
+    with engine.compile(tape, opts) as a, \
+            engine.compile(tape, opts.with_engine_option("cuda", "gridBlocksPerSm", "1")) as b:
+        assert b.info()["grid"] == b.info()["sm_count"]
+        a.setInputs(x)
+        b.setInputs(x)
+        whole, _ = a.replay_sums(total, off, seed)
+        small_grid, _ = b.replay_sums(total, off, seed)
+        rng = np.random.default_rng(3)
+        cuts = np.sort(rng.choice(np.arange(1, total // 32), size=9, replace=False)) * 32
+        bounds = [0, *cuts.tolist(), total]
+        pieces = [(off + lo, hi - lo) for lo, hi in zip(bounds[:-1], bounds[1:])]
+        rng.shuffle(pieces)
+        accumulated = _accumulate(a, pieces, seed)
+        sharded, _ = a.replaySharded_sums(total, off, seed, chunk_paths=(1 << 17) + 5)
+    np.testing.assert_array_equal(small_grid, whole)
+    np.testing.assert_array_equal(accumulated, whole)
+    np.testing.assert_array_equal(sharded, whole)
 
 
 def test_full_size_properties(engine):
     """At 1e8 paths: replay is a pure function of the range (two calls are
-    bit-identical) and is additive over a split of the range."""
+    bit-identical), and four quarters accumulated on the device give the
+    whole range's bits."""
     tape = quant.asian_tape(252)
     n = 100_000_000
     with engine.compile(tape, FP64) as ex:
         whole, _ = ex.replay_sums(n, 0, 42)
         again, _ = ex.replay_sums(n, 0, 42)
-        parts = sum(ex.replay_sums(n // 4, k * (n // 4), 42)[0] for k in range(4))
+        parts = _accumulate(ex, [(k * (n // 4), n // 4) for k in range(4)], 42)
     np.testing.assert_array_equal(whole, again)
-    np.testing.assert_allclose(parts, whole, rtol=1e-13)
+    np.testing.assert_array_equal(parts, whole)
     mean = whole[0] / n
     assert abs(mean - 5.3017) < 5e-3
-
-
-def test_sharded_single_rank_matches_replay(engine):
-    tape = quant.asian_tape(252)
-    with engine.compile(tape, FP64) as ex:
-        a = ex.replaySharded(10_000_000, 3, 42, chunk_paths=1 << 20)
-        b = ex.replay(10_000_000, 3, 42)
-    assert a.value() == pytest.approx(b.value(), rel=1e-13)
-    np.testing.assert_allclose(a.gradients(), b.gradients(), rtol=1e-13)
 
 
 def test_no_spill_and_plan(engine):
@@ -471,12 +572,12 @@ def test_barrier_fast_fp32_price_within_1e5(engine, oracle_mod):
 
 
 def test_fp32_asian_bit_stable_and_close(engine, oracle_mod):
-    """Fp32BackendComparisonTest: repeat runs are bit-identical; offset bursts
+    """Fp32BackendComparisonTest: 60 repeat runs are bit-identical; offset bursts
     stay finite; price/delta/vega within 1e-5 of the fp64 oracle."""
     tape = fp32_asian_50(50)
     with engine.compile(tape, FP32) as ex:
         first, _ = ex.replay_sums(1_000_000, 0, 0xA51A17)
-        for _ in range(5):
+        for _ in range(60):  # Fp32BackendComparisonTest.java:54 settles 60 repeats
             again, _ = ex.replay_sums(1_000_000, 0, 0xA51A17)
             np.testing.assert_array_equal(first, again)
         for k in range(25):
