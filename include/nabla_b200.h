@@ -325,6 +325,13 @@ int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint6
 int nt_replay_sharded_async(nt_exec* exec, uint64_t total_paths, uint64_t path_offset,
                             uint64_t seed, uint64_t chunk_paths);
 
+/* Device time in milliseconds (CUDA events on the executable's stream) of
+ * the last all-reduce nt_replay_sharded(_async) enqueued; waits for it.
+ * NT_E_STATE before the first one.  The kernelStats-style figure that tells
+ * the collective's share of a sharded step.  No counterpart in the reference
+ * (it has no multi-GPU path). */
+int nt_dist_collective_ms(nt_exec* exec, double* ms);
+
 /* Leaves the communicator (ncclCommDestroy). */
 int nt_dist_detach(nt_exec* exec);
 
@@ -362,15 +369,6 @@ int nt_fma_peak(int32_t device, int32_t fp64, int32_t iters, double* tflops);
  * figure would credit clocks the long run cannot hold).  No counterpart in
  * the reference. */
 int nt_fma_peak_sustained(int32_t device, int32_t fp64, int32_t millis, double* tflops);
-
-/* Launches one math-probe kernel (148*4 blocks of 256 threads, `iters` calls
- * each) for instruction / flop counting under ncu: which = 0 empty loop,
- * 1 library exp, 2 library log, 3 library sincos, 4 library sqrt, 5 the
- * replay's full-range exp, 6 its series -2 ln(u1), 7 its series sincos(2 pi u2),
- * 8 library exp on a wide range, 9 the table-driven -2 ln(u1), 10 the
- * table-driven sincos(2 pi u2), 11 the radius sqrt, 12 the series exp
- * (|x| <= 1/8), 13 one Philox2x32-10 block.  No counterpart in the reference. */
-int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 
 /* Evaluates one of the replay's dedicated fp64 routines on the device over n
  * host inputs (copied in and out), so the tests can measure their accuracy as

@@ -115,24 +115,12 @@ SIGNATURES = {
                          ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32), _f64p], ctypes.c_int),
     "nt_fma_peak": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
     "nt_fma_peak_sustained": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
-    "nt_math_probe": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f64p], ctypes.c_int),
+    "nt_dist_collective_ms": ([ctypes.c_void_p, _f64p], ctypes.c_int),
     "nt_math_eval": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint32), _f64p, _f64p,
                       _f64p], ctypes.c_int),
     "nt_replay_noalloc": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
                            ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
-
-MATH_PROBES = {0: "loop", 1: "exp(lib, |x|<=1/8)", 2: "log(lib)", 3: "sincos(lib)", 4: "sqrt(lib)",
-               5: "exp(full range)", 6: "-2ln(u1)(series)", 7: "sincos(2pi u2)(series)", 8: "exp(lib, |x|<=4)",
-               9: "-2ln(u1)(table)", 10: "sincos(2pi u2)(table)", 11: "sqrt(replay radius)",
-               12: "exp(series, |x|<=1/8)", 13: "philox2x32-10 block"}
-
-
-def math_probe(device: int, which: int, iters: int) -> float:
-    out = ctypes.c_double(0.0)
-    check(lib().nt_math_probe(device, which, iters, ctypes.byref(out)))
-    return out.value
-
 
 def math_eval(device: int, which: int, words=None, x=None):
     """nt_math_eval: one of the replay's fp64 routines on the device over the

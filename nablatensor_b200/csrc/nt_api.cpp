@@ -223,6 +223,15 @@ int nt_shard_range(uint64_t total_paths, uint64_t path_offset, int32_t nranks, i
   });
 }
 
+int nt_dist_collective_ms(nt_exec* exec, double* ms) {
+  return guarded([&] {
+    nt::Exec& x = impl(exec);
+    std::lock_guard<std::mutex> lk(x.mu);
+    if (!ms) nt::fail(NT_E_INVALID_ARG, "ms is null");
+    *ms = x.collective_ms();
+  });
+}
+
 int nt_dist_detach(nt_exec* exec) {
   return guarded([&] {
     nt::Exec& x = impl(exec);
@@ -241,14 +250,6 @@ extern "C" int nt_philox_words(int32_t device, uint64_t path0, uint32_t n_paths,
 extern "C" int nt_replay_noalloc(nt_exec* exec, uint64_t paths, uint64_t path_offset, uint64_t seed,
                                  const double* d_inputs, double* d_sums, void* stream) {
   return guarded([&] { nt::replay_noalloc(exec, paths, path_offset, seed, d_inputs, d_sums, stream); });
-}
-
-extern "C" int nt_math_probe(int32_t device, int32_t which, int32_t iters, double* checksum) {
-  return guarded([&] {
-    if (which < 0 || which > 13) nt::fail(NT_E_INVALID_ARG, "which must be in [0, 13]");
-    if (iters <= 0) nt::fail(NT_E_INVALID_ARG, "iters must be positive");
-    nt::math_probe(device, which, iters, checksum);
-  });
 }
 
 extern "C" int nt_math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x,

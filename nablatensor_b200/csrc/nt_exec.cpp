@@ -223,7 +223,8 @@ void Exec::load(int max_regs) {
   cuda_check(cudaMemset(d_glim, 0, words), "cudaMemset exact words");
   cuda_check(cudaMemset(d_ticket, 0, sizeof(unsigned int)), "cudaMemset ticket");
   cuda_check(cudaMemset(d_acc, 0, words), "cudaMemset accumulator");
-  cuda_check(cudaEventCreateWithFlags(&ev_shard, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaEventCreate(&ev_shard), "cudaEventCreate");
+  cuda_check(cudaEventCreate(&ev_reduced), "cudaEventCreate");
   if (cfg.global_ckpt && ckpt_values(plan) > 0) {
     const size_t bytes = (size_t)ckpt_values(plan) * grid * cfg.block * (cfg.f32 ? 4 : 8);
     cuda_check(cudaMalloc(&d_gck, bytes), "cudaMalloc checkpoints");
@@ -287,6 +288,7 @@ Exec::~Exec() {
   if (h_stage) cudaFreeHost(h_stage);
   if (h_words) cudaFreeHost(h_words);
   if (ev_shard) cudaEventDestroy(ev_shard);
+  if (ev_reduced) cudaEventDestroy(ev_reduced);
   if (stream) cudaStreamDestroy(stream);
   if (module) driver().moduleUnload(module);
   if (mk_module) driver().moduleUnload(mk_module);
@@ -492,7 +494,18 @@ void Exec::sharded_enqueue(uint64_t total, uint64_t offset, uint64_t seed, uint6
     // GPUs.
     cuda_check(cudaEventRecord(ev_shard, stream), "cudaEventRecord");
     comm->allreduce_i64(d_acc, (size_t)channels * kXWords, (void*)stream);
+    cuda_check(cudaEventRecord(ev_reduced, stream), "cudaEventRecord");
+    reduced_once = true;
   }
+}
+
+double Exec::collective_ms() {
+  if (!reduced_once) fail(NT_E_STATE, "no all-reduce has run on this executable");
+  bind();
+  cuda_check(cudaEventSynchronize(ev_reduced), "cudaEventSynchronize");
+  float ms = 0.0f;
+  cuda_check(cudaEventElapsedTime(&ms, ev_shard, ev_reduced), "cudaEventElapsedTime");
+  return ms;
 }
 
 void Exec::sharded(uint64_t total, uint64_t offset, uint64_t seed, uint64_t chunk, double* sums, double* seconds) {

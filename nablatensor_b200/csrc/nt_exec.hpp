@@ -42,6 +42,8 @@ struct Exec {
   double* h_stage = nullptr;    // pinned: inputs, then sums
   long long* h_words = nullptr; // pinned: the accumulator's words on their way to the host
   cudaEvent_t ev_shard = nullptr;  // recorded once this rank's shard is enqueued, before the all-reduce
+  cudaEvent_t ev_reduced = nullptr;  // recorded after the all-reduce (timing: ev_shard -> ev_reduced)
+  bool reduced_once = false;
   std::vector<double> inputs;
   bool dirty = true;
   double compile_seconds = 0.0;
@@ -89,6 +91,8 @@ struct Exec {
   void markets(int32_t n_states, const double* inputs, uint64_t paths, uint64_t offset, uint64_t seed,
                double* sums, double* seconds);
   void detach();
+  // Device time of the last all-reduce (waits for it), in milliseconds.
+  double collective_ms();
 };
 
 }  // namespace nt

@@ -172,8 +172,6 @@ extern const char* kExactSource;          // nt_exact.cuh, embedded at build tim
 // (nt_flops.cpp), used for the algorithmic flop count of a tape.
 extern const double kFlopWeights[4];
 
-// Math probe launches (per-call counts under ncu).
-void math_probe(int32_t device, int32_t which, int32_t iters, double* checksum);
 void math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x, double* out0,
                double* out1);
 
