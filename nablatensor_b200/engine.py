@@ -4,8 +4,9 @@ Mirrors nablatensor-core/.../engine/{AadEngine,AadExecutable,AbstractAadExecutab
 AadResult,AadTotals,AadOptions,AadEngines}.java: same names, argument meaning
 and error behaviour (ValueError for IllegalArgumentException, RuntimeError for
 IllegalStateException, NotImplementedError for UnsupportedOperationException).
-The engine registered here is "cuda" (priority 100, the reference's
-CudaAadEngine slot, CudaAadEngine.java:26-34) and is backed by
+The engine registered here is "cuda" (priority 110, above the reference's
+CudaAadEngine at 100, CudaAadEngine.java:26-34, so that a name lookup finds it
+first, as the Java module java/nablatensor-engine-b200 does) and is backed by
 libnabla_b200.so; there is no CPU fallback once it is selected.
 """
 from __future__ import annotations
@@ -180,7 +181,9 @@ class B200AadExecutable(AadExecutable):
         self._closed = True
         knobs = {}
         for k, v in options.engine_options_for("cuda").items():
-            if k in _ENGINE_KEYS:
+            if k == "device":
+                device = int(v)
+            elif k in _ENGINE_KEYS:
                 knobs[_ENGINE_KEYS[k]] = int(v)
             elif k in _ENGINE_FLAGS and str(v).lower() in ("1", "true", "on"):
                 flags |= _ENGINE_FLAGS[k]
@@ -197,7 +200,12 @@ class B200AadExecutable(AadExecutable):
         self._inputs = tape.recordedInputs()
         self._channels = tape.output_count() * (2 + tape.input_count())
         self._pps = 0.0
-        self._max_chunk_seconds = 2.0
+        # calibrate() grows its probes x8 until one takes a fifth of the budget;
+        # at ~1e9 scenarios/s the reference's 2 s budget would spend about 2 s
+        # on probes, while a chunk costs only one more launch here (the chunks
+        # accumulate on the device), so the budget is 20 ms -- the Java
+        # module's defaultMaxChunkSeconds() override.
+        self._max_chunk_seconds = 0.02
         info = _lib.NtExecInfo()
         _lib.check(_lib.lib().nt_exec_info_get(self._h, ctypes.byref(info)))
         self._info = info.as_dict()
@@ -442,7 +450,7 @@ class CudaAadEngine(AadEngine):
         return "cuda"
 
     def priority(self) -> int:
-        return 100
+        return 110
 
     def isAvailable(self) -> bool:
         """Never raises (AadEngine.java:39-40)."""

@@ -174,15 +174,6 @@ def test_ctypes_layouts_follow_the_header(struct, cls):
     assert [name for name, _ in cls._fields_] == _header_fields(struct)
 
 
-def test_java_options_layout_follows_the_header():
-    """The FFM StructLayout shown to integrators names every nt_options field
-    in order (a missing trailing field would be read from past the end)."""
-    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
-        text = f.read()
-    layout = re.search(r"StructLayout OPTIONS = MemoryLayout\.structLayout\((.*?)\);", text, re.S).group(1)
-    assert re.findall(r'withName\("(\w+)"\)', layout) == _header_fields("nt_options")
-
-
 def test_math_eval_rejects_bad_arguments_before_touching_a_device(ntlib):
     L = _lib.lib()
     out = np.zeros(4)
