@@ -144,11 +144,11 @@ void Exec::load(int max_regs) {
              "cuFuncSetAttribute");
   int regs = 0, local = 0, ssm = 0;
   cu_check(d.funcGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, function), "cuFuncGetAttribute");
-  if (auto_regs && regs >= 255) {
-    // The register file ran out: the kernel spills at any occupancy, and a
-    // latency-bound sweep gains more from twice the resident warps than it
-    // loses to further spills (a 118-unit CVA book: +56 %).  Recompile with
-    // a cap of 128 registers.
+  if (auto_regs && regs >= 248) {
+    // The register file ran out (or came within a granule of it): one block
+    // of 64 threads per quarter SM, and a latency-bound sweep gains more from
+    // twice the resident warps than it loses to spills (a 118-unit CVA book:
+    // +56 %).  Recompile with a cap of 128 registers.
     double secs2 = 0.0;
     cfg.max_regs = 128;
     source = emit(tape, plan, cfg);
@@ -165,12 +165,13 @@ void Exec::load(int max_regs) {
   }
   cu_check(d.funcGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, function), "cuFuncGetAttribute");
   if (auto_seg && cfg.global_ckpt && plan.loop.present && plan.loop.G == 1 && plan.loop.K >= 4 && regs <= 192 &&
-      local == 0) {
+      local <= 64) {
     // A heavy unit (one unit per segment) whose kernel left registers
-    // unused: two units per segment give the reverse sweep two units of
-    // independent work to overlap (the 10-asset basket: +17 %).  Kept when
-    // the wider kernel still fits in 255 registers without spilling; the
-    // choice depends only on the compiler's register count, never on timing.
+    // unused (a few spilled words aside): two units per segment give the
+    // reverse sweep two units of independent work to overlap (the 10-asset
+    // basket: +17 %).  Kept when the wider kernel still fits in 255 registers
+    // and spills no more; the choice depends only on the compiler's register
+    // and local-memory counts, never on timing.
     EmitConfig c2 = cfg;
     c2.seg_units = 2;
     Plan p2 = plan_tape(tape, c2);
@@ -193,7 +194,7 @@ void Exec::load(int max_regs) {
       } catch (const Error&) {
         regs2 = 255;
       }
-      if (m2 && regs2 < 255 && local2 == 0) {
+      if (m2 && regs2 < 255 && local2 <= local) {
         cu_check(d.moduleUnload(module), "cuModuleUnload");
         module = m2;
         function = f2;
