@@ -322,6 +322,51 @@ NT_FN double nt_sqrt_pos(double a) {
 #endif
 }
 
+/*
+ * exp for fp32 tapes, whose nodes the reference rounds to float after
+ * evaluating exp in double ((float)Math.exp(x), ScalarReplay.java:37-51).  A
+ * float result needs far less than a double's accuracy: evaluated in double
+ * to about 2^-43 relative (q of degree 7 on the Cody-Waite range, the
+ * construction of nt_exp_cw), the rounding to float is the reference's
+ * except when e^x lies within 2^-43 of a float rounding boundary, about one
+ * argument in 2^19.  x is clamped in single precision to [-105, 89], beyond
+ * which the float result is 0 or +inf anyway, so 2^k is applied by adding k
+ * to p's exponent (p * 2^k stays a normal double) and the one rounding to
+ * float handles overflow and float subnormals.  NaN passes through.
+ */
+NT_FN float nt_exp_f32(float x) {
+  const double d = (double)fminf(fmaxf(x, -105.0f), 89.0f);
+  const double kt = fma(d, 0x1.71547652b82fep+0 /* 1/ln2 */, 0x1.8p52);
+  const double kd = kt - 0x1.8p52;
+  const int k = (int)nt_loword(kt);
+  double r = fma(kd, -0x1.62e42fefa3800p-1 /* ln2 hi */, d);
+  r = fma(kd, -0x1.ef35793c76730p-45 /* ln2 lo */, r);
+  double q = NT_EXPF_C7;
+  q = fma(q, r, NT_EXPF_C6);
+  q = fma(q, r, NT_EXPF_C5);
+  q = fma(q, r, NT_EXPF_C4);
+  q = fma(q, r, NT_EXPF_C3);
+  q = fma(q, r, NT_EXPF_C2);
+  q = fma(q, r, NT_EXPF_C1);
+  q = fma(q, r, NT_EXPF_C0);
+  const double p = fma(fma(q, r, 1.0), r, 1.0);
+  const double y = nt_from_words(nt_hiword(p) + (int)((unsigned)k << 20), nt_loword(p));
+  return x != x ? x : (float)y;
+}
+
+/* The float-result exp for |x| <= 1/8 (a GBM log-return): the series form of
+ * nt_exp_small with q of degree 5, about 2^-43 relative. */
+NT_FN float nt_exp_f32s(float x) {
+  const double d = (double)x;
+  double q = NT_EXPFS_C5;
+  q = fma(q, d, NT_EXPFS_C4);
+  q = fma(q, d, NT_EXPFS_C3);
+  q = fma(q, d, NT_EXPFS_C2);
+  q = fma(q, d, NT_EXPFS_C1);
+  q = fma(q, d, NT_EXPFS_C0);
+  return (float)fma(fma(q, d, 1.0), d, 1.0);
+}
+
 #ifndef NT_HOST
 /* nt_exp_cw that also records in `wide` whether this lane's argument left the
  * series range: the redo pass of the forward loop (see NT_EXP64F), after
@@ -329,6 +374,17 @@ NT_FN double nt_sqrt_pos(double a) {
 NT_FN double nt_exp_cw_flag(double x, bool& wide) {
   wide |= !(fabs(x) <= 0.125);
   return nt_exp_cw(x);
+}
+
+/* The float-result forms' flagging twins (see nt_exp_series_flag). */
+NT_FN float nt_exp_f32s_flag(float x, bool& wide) {
+  wide |= !(fabsf(x) <= 0.125f);
+  return nt_exp_f32s(x);
+}
+
+NT_FN float nt_exp_f32_flag(float x, bool& wide) {
+  wide |= !(fabsf(x) <= 0.125f);
+  return nt_exp_f32(x);
 }
 #endif
 
@@ -350,17 +406,27 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
  * loop's form for an exp the reverse sweep recomputes (the bare series, wide
  * arguments recorded in nt_wide), NT_EXP64W the redo pass's (full range,
  * recording too); NT_EXP64_SERIES is the recompute once the forward sweep has
- * shown every argument of the warp in the series range. */
+ * shown every argument of the warp in the series range.  NT_EXPF32... are the
+ * same four forms for fp32 tapes under the reference's fp32 semantics, with
+ * float arguments and results (nt_exp_f32, nt_exp_f32s). */
 #ifdef NT_HOST
 #define NT_EXP64(x) exp(x)
 #define NT_EXP64W(x) exp(x)
 #define NT_EXP64F(x) exp(x)
 #define NT_EXP64_SERIES(x) exp(x)
+#define NT_EXPF32(x) ((float)exp((double)(x)))
+#define NT_EXPF32W(x) ((float)exp((double)(x)))
+#define NT_EXPF32F(x) ((float)exp((double)(x)))
+#define NT_EXPF32_SERIES(x) ((float)exp((double)(x)))
 #else
 #define NT_EXP64(x) nt_exp_cw(x)
 #define NT_EXP64W(x) nt_exp_cw_flag((x), nt_wide)
 #define NT_EXP64F(x) nt_exp_series_flag((x), nt_wide)
 #define NT_EXP64_SERIES(x) nt_exp_small(x)
+#define NT_EXPF32(x) nt_exp_f32(x)
+#define NT_EXPF32W(x) nt_exp_f32_flag((x), nt_wide)
+#define NT_EXPF32F(x) nt_exp_f32s_flag((x), nt_wide)
+#define NT_EXPF32_SERIES(x) nt_exp_f32s(x)
 #endif
 
 /* ---- table-driven Box-Muller ---------------------------------------------

@@ -165,8 +165,11 @@ std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B
     case NT_DIV: return A + " / " + B;
     case NT_NEG: return "-" + A;
     case NT_EXP: {
-      const std::string e = exp_fn_;
-      return cfg_.wide32 ? "((float)" + e + "(double)" + A + "))" : R(e.c_str(), "expf(") + A + ")";
+      // fp32 tapes under the reference's fp32 semantics take the float-result
+      // forms (NT_EXPF32...): evaluated in double, rounded once to float.
+      const std::string e64 = exp_fn_;
+      if (!cfg_.wide32) return R(e64.c_str(), "expf(") + A + ")";
+      return "NT_EXPF32" + e64.substr(std::string("NT_EXP64").size()) + A + ")";
     }
     case NT_LOG: return cfg_.wide32 ? "((float)log((double)" + A + "))" : R("log(", "logf(") + A + ")";
     case NT_SQRT: return R("sqrt(", "sqrtf(") + A + ")";
