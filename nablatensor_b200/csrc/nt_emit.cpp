@@ -17,6 +17,7 @@
 // (nablatensor-engine-cpu/.../cpu/ScalarReplay.java:129-171), emitted only for
 // contributions into active arguments as the reference device sweep does
 // (nablatensor-core/.../CudaAadCodegen.java:386-448).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -394,12 +395,28 @@ void Emitter::emit_body_reverse(int g) {
   auto adj = [&](const Ref& r, bool* active) -> std::string {
     if (r.kind == REF_SAME) { *active = lp_.body[r.idx].active; return "b" + std::to_string(r.idx); }
     if (r.kind == REF_CARRY) { *active = lp_.body[r.idx].active; return "n" + std::to_string(r.idx); }
-    if (r.kind == REF_GATHER) { *active = gather_active(r.idx); return "nt_gd" + std::to_string(r.idx) + "[" + unit + "]"; }
+    if (r.kind == REF_GATHER) { *active = gather_active(r.idx); return "gd" + std::to_string(r.idx); }
     *active = t_.active[r.idx] != 0;
     return "d" + std::to_string(r.idx);
   };
   o_.open("{");
   zero_.clear();  // the unit's own registers start at zero; outer ones never do here
+  // A gathered argument's adjoint collects the unit's contributions in a
+  // register (in the interpreter's order) and is stored to the unit's slot
+  // once, at the end of the unit: one local store per unit instead of a
+  // load and a store per contribution.
+  std::vector<int32_t> gathered;
+  for (int32_t j = 0; j < L; ++j) {
+    const BodyNode& bn = lp_.body[j];
+    for (const Ref* r : {&bn.ra, &bn.rb})
+      if (r->kind == REF_GATHER && gather_active(r->idx) &&
+          std::find(gathered.begin(), gathered.end(), r->idx) == gathered.end())
+        gathered.push_back(r->idx);
+  }
+  for (int32_t k : gathered) {
+    o_.line("real gd" + std::to_string(k) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+    zero_.insert("gd" + std::to_string(k));
+  }
   for (int32_t j = 0; j < L; ++j) {
     const BodyNode& bn = lp_.body[j];
     if (!bn.active) continue;
@@ -428,6 +445,7 @@ void Emitter::emit_body_reverse(int g) {
     if (lp_.body[k].active) o_.line("cd" + std::to_string(k) + " = n" + std::to_string(k) + ";");
   for (int32_t j : lp_.exits)
     if (!lp_.is_carry[j] && lp_.body[j].active) o_.line("xd" + std::to_string(j) + " = " + (cfg_.f32 ? "0.0f;" : "0.0;"));
+  for (int32_t k : gathered) o_.line("nt_gd" + std::to_string(k) + "[" + unit + "] = gd" + std::to_string(k) + ";");
   zero_.clear();
   o_.close();
 }
@@ -469,9 +487,11 @@ void Emitter::emit_reverse_for_output(int o) {
     zero_.clear();  // the segment loop runs its code more than once
     const int32_t L = lp_.L, G = lp_.G, K = lp_.K;
     const int32_t nck = (int32_t)lp_.ckpt.size();
+    // Every unit stores its slot of each active gathered adjoint (see
+    // emit_body_reverse), so the arrays need no initial zeroing.
     for (size_t k = 0; k < lp_.gather.size(); ++k)
       if (gather_active((int32_t)k))
-        o_.line("real nt_gd" + std::to_string(k) + "[" + std::to_string(lp_.N) + "] = {};");
+        o_.line("real nt_gd" + std::to_string(k) + "[" + std::to_string(lp_.N) + "];");
     if (cfg_.target != 1 && cfg_.rev_unroll > 1) o_.line("#pragma unroll " + std::to_string(cfg_.rev_unroll));
     o_.open("for (int s = " + std::to_string(K - 1) + "; s >= 0; --s) {");
     for (int32_t c = 0; c < nck; ++c)
