@@ -68,9 +68,11 @@ class Emitter {
 
  private:
   // The block's exact words live in shared memory while they take at most
-  // 24 KB (44 channels of 69 words); beyond that the kernel adds its tile
-  // sums to the launch's words in global memory.
-  bool xshared() const { return (int64_t)channels() * kXWords * 8 <= 24 * 1024; }
+  // 8 KB (14 channels of 69 words: the Asian's 7 take 3.9 KB); beyond that
+  // the kernel adds its tile sums to the launch's words in global memory, so
+  // that many-input tapes with small, register-heavy blocks (the CVA book's
+  // 43 channels, 64 threads) keep their resident blocks.
+  bool xshared() const { return (int64_t)channels() * kXWords * 8 <= 8 * 1024; }
   const Tape& t_;
   const Plan& p_;
   const Loop& lp_;
