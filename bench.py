@@ -350,7 +350,7 @@ def roofline_of(wl: "Workload", info: dict, peaks: Peaks, kernel_s: float, paths
 
 
 def measure(args, wl: "Workload", rank: int, world: int, local_rank: int, peaks: Peaks, steps: int, warmup: int,
-            barrier, max_over_ranks, total=None, chunk=None) -> dict:
+            barrier, max_over_ranks, total=None, chunk=None, engine_options=None) -> dict:
     """Times one workload: `steps` device-timed steps (CUDA events on the
     engine's stream, inputs resident, L2 flushed between steps, max over
     ranks), then the same steps end to end through the C ABI with host inputs
@@ -363,7 +363,10 @@ def measure(args, wl: "Workload", rank: int, world: int, local_rank: int, peaks:
     tape = wl.tape()
     x = wl.inputs(tape)
     precision = PrecisionEnum.FLOAT32 if wl.f32 else PrecisionEnum.FLOAT64
-    ex = CudaAadEngine(device=local_rank).compile(tape, AadOptions(precision=precision))
+    options = AadOptions(precision=precision)
+    for k, v in (engine_options or {}).items():
+        options = options.with_engine_option("cuda", k, v)
+    ex = CudaAadEngine(device=local_rank).compile(tape, options)
     try:
         ex.setInputs(x)
         info = ex.info()
@@ -474,6 +477,20 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
     peaks = Peaks(local_rank)
     m = measure(args, wl, rank, world, local_rank, peaks, args.steps, args.warmup, barrier, max_over_ranks,
                 total=args.paths, chunk=args.chunk)
+    # The storage plan, re-checked on the headline: the default (normals taped,
+    # GBM exps recomputed) against recompute-all (nothing taped, Box-Muller
+    # and exps recomputed in the reverse sweep), 3 steps each.  Under the
+    # power cap the clock differs between them, so time x median SM clock
+    # is reported beside the rate.
+    plans = {}
+    if world == 1 and not args.no_configs and wl.name == "asian1e9":
+        alt = measure(args, wl, rank, world, local_rank, peaks, 3, 3, barrier, max_over_ranks,
+                      total=args.paths, chunk=args.chunk, engine_options={"recomputeAll": "1"})
+        for name, r in (("default", m), ("recomputeAll", alt)):
+            mhz = r["clocks"].get("sm_mhz")
+            plans[name] = {"value": r["value"], "ms_per_step": r["ms_per_step"], "sm_mhz": mhz,
+                           "ms_x_ghz": r["ms_per_step"] * mhz / 1e3 if mhz else None,
+                           "tape_slots": r["kernel"]["tape_slots"], "registers": r["kernel"]["registers"]}
     # The other benchmark configurations, on one GPU only: a few steps each,
     # the same measurement, under one key of the same line.
     others = {}
@@ -516,6 +533,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
             line["collective"] = m["collective"]
         if others:
             line["configs"] = others
+        if plans:
+            line["plans"] = plans
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
