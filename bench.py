@@ -442,10 +442,14 @@ def measure(args, wl: "Workload", rank: int, world: int, local_rank: int, peaks:
                "_tape": tape, "_x": x}
         if world > 1:
             cm = max_over_ranks(collective_ms[-1])
-            out["collective"] = {"ms_last_step": cm, "share_of_step": cm / (total_ms / steps),
-                                 "what": "device time of the int64 all-reduce of the exact accumulator words "
+            cmin = -max_over_ranks(-collective_ms[-1])
+            out["collective"] = {"ms_last_step_max": cm, "ms_last_step_min": cmin,
+                                 "share_of_step": cm / (total_ms / steps),
+                                 "what": "device time from the end of a rank's shard to the end of the int64 "
+                                         "all-reduce of the exact accumulator words "
                                          f"({info['channels']} channels x 69 words), CUDA events on the engine's "
-                                         "stream, max over ranks"}
+                                         "stream: the max over ranks includes waiting for the slowest rank's "
+                                         "shard, the min (the slowest rank's own) is the collective alone"}
         if world > 1:
             ex.distDetach()
         return out
