@@ -563,6 +563,60 @@ NT_FN void nt_bm64(nt_u32 w0, nt_u32 w1, double* cos_leg, double* sin_leg) {
 #endif
 }
 
+#ifndef NT_HOST
+/* ---- float-result Box-Muller ---------------------------------------------
+ * For fp32 tapes under the reference's fp32 semantics, where each normal is
+ * the double Box-Muller value rounded to float.  A value that is only ever
+ * narrowed needs about 2^-40 relative, not a double's 2^-53, so the radius
+ * stops earlier than the fp64 routines above (same tables, same reduction):
+ *   -2 ln u1: the series to v^5 (truncation below 2^-40.5 of the result) and
+ *     one rounding of k (-2 ln 2) + (-2 ln c_j), the table's low part unused;
+ *   the radius: one coupled Newton step from the hardware rsqrt (relative
+ *     error 1.5 e^2 for a seed error e).
+ * The angle keeps the fp64 sin and cos: near a zero of cos or sin the leg is
+ * a difference of two products, and a shorter series would leave its
+ * truncation as an absolute error, far above 2^-40 of a small leg.  The
+ * narrowed legs are the narrowed fp64 legs except where the double value lies
+ * within about 2^-40 of a float rounding boundary, there one float ulp away
+ * (measured on the device against the fp64 legs: tests/test_gpu_math.py). */
+NT_FN double nt_neg2log_u1_f(nt_u32 w0) {
+  const double u = fma((double)w0, 0x1p-32, 0x1p-33); /* (w0 + 0.5) 2^-32, exact */
+  const int hi = nt_hiword(u);
+  const int f20 = hi & 0x000fffff;
+  const bool fold = f20 >= 0x00080000;
+  const int k = (hi >> 20) - (fold ? 1022 : 1023);
+  const int mhi = f20 | (fold ? 0x3fe00000 : 0x3ff00000);
+  const int j = fold ? (f20 - 0x00080000 + 0x2000) >> 14 : 32 + ((f20 + 0x1000) >> 13);
+  const int chi = fold ? (mhi + 0x2000) & ~0x3fff : (mhi + 0x1000) & ~0x1fff;
+  const double m = nt_from_words(mhi, nt_loword(u));
+  double rc, lh;
+  nt_tab2(NT_LN_TAB, j, &rc, &lh);
+  const double v = (m - nt_from_words(chi, 0u)) * rc; /* m - c_j exact */
+  double p = 1.0 / 80.0;
+  p = fma(p, v, 1.0 / 32.0);
+  p = fma(p, v, 1.0 / 12.0);
+  p = fma(p, v, 0.25);
+  const double g = fma(v * v, p, v);
+  return fma((double)k, -0x1.62e42fefa39efp+0 /* -2 ln 2 */, lh) + g;
+}
+
+NT_FN double nt_sqrt_pos_f(double a) {
+  double y;
+  asm("rsqrt.approx.ftz.f64 %0, %1;" : "=d"(y) : "d"(a));
+  const double g = a * y;
+  const double r = fma(-g, 0.5 * y, 0.5);
+  return fma(g, r, g);
+}
+
+NT_FN void nt_bm64f_words(nt_u32 w0, nt_u32 w1, float* cos_leg, float* sin_leg) {
+  const double r = nt_sqrt_pos_f(nt_neg2log_u1_f(w0));
+  double s, c;
+  nt_sincos_2pi_u2_t(w1, &s, &c);
+  *cos_leg = (float)(r * c);
+  *sin_leg = (float)(r * s);
+}
+#endif
+
 /* fp32 Box-Muller: the uint32 words are the fp64 generator's; u1 is rounded
  * to the nearest float and clamped below 1 so the radius never collapses. */
 NT_FN void nt_bm32(nt_u32 w0, nt_u32 w1, float* cos_leg, float* sin_leg) {
@@ -597,12 +651,19 @@ NT_FN void nt_normal_pair32(nt_key k, nt_u32 pair, float* c, float* s) {
 }
 
 /* fp32 pair evaluated in fp64 and narrowed: the reference's fp32 semantics
- * (each stored value is the double result rounded to float). */
+ * (each stored value is the double result rounded to float); on the device
+ * by the float-result routines. */
 NT_FN void nt_normal_pair32w(nt_key k, nt_u32 pair, float* c, float* s) {
+#ifdef NT_HOST
   double cd, sd;
   nt_normal_pair64(k, pair, &cd, &sd);
   *c = (float)cd;
   *s = (float)sd;
+#else
+  nt_u32 w0, w1;
+  nt_normal_words(k, pair, &w0, &w1);
+  nt_bm64f_words(w0, w1, c, s);
+#endif
 }
 
 NT_FN float nt_normal32w(nt_key k, nt_u32 ordinal) {
@@ -697,6 +758,24 @@ NT_FN double nt_min64(double a, double b) {
   if (a != a) return a;
   if (a == 0.0 && b == 0.0 && nt_signbit64(b)) return b;
   return a <= b ? a : b;
+}
+
+/* 1 / x correctly rounded: the bits of the IEEE division 1.0f / x. */
+NT_FN float nt_rcp32(float x) {
+#ifdef NT_HOST
+  return 1.0f / x;
+#else
+  return __frcp_rn(x);
+#endif
+}
+
+/* a * b rounded once, never contracted into a neighbouring add. */
+NT_FN float nt_fmul_rn(float a, float b) {
+#ifdef NT_HOST
+  return a * b;
+#else
+  return __fmul_rn(a, b);
+#endif
 }
 
 NT_FN float nt_max32(float a, float b) {

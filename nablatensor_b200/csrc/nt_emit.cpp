@@ -144,11 +144,22 @@ class Emitter {
     return false;
   }
 
-  std::string fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a) const;
+  std::string fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a,
+                       bool a_one = false) const;
+  // The node is the constant 1 (in every unit, for a loop node): a division
+  // by it is a reciprocal.
+  bool node_is_one(int32_t x) const { return t_.op[x] == NT_CONST && t_.c[x] == 1.0; }
+  bool ref_is_one(const Ref& r) const {
+    if (r.kind == REF_SAME) {
+      const BodyNode& n = lp_.body[r.idx];
+      return n.op == NT_CONST && n.cslot < 0 && n.c == 1.0;
+    }
+    return r.kind == REF_OUT && node_is_one(r.idx);
+  }
   void emit_straight_forward(int32_t lo, int32_t hi);
   void emit_straight_reverse(int32_t lo, int32_t hi);
   void emit_rule(int op, const std::string& D, const std::string& Va, const std::string& Vb,
-                 const std::string& Vi, const std::string* da, const std::string* db);
+                 const std::string& Vi, const std::string* da, const std::string* db, bool a_one = false);
   void emit_body_forward(const std::string& pre, const std::string& unit, bool recompute, int g);
   void emit_body_reverse(int g);
   void emit_scenario();
@@ -158,14 +169,19 @@ class Emitter {
   void acc_line(int32_t k, const std::string& x);
 };
 
-std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a) const {
+std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B, double c, int32_t a,
+                              bool a_one) const {
   switch (op) {
     case NT_CONST: return lit(c, cfg_.f32);
     case NT_INPUT: return "in" + std::to_string(a);
     case NT_ADD: return A + " + " + B;
     case NT_SUB: return A + " - " + B;
     case NT_MUL: return A + " * " + B;
-    case NT_DIV: return A + " / " + B;
+    case NT_DIV:
+      // 1 / x in single precision: the correctly rounded reciprocal, the bits
+      // of the IEEE division without its general-quotient path.
+      if (cfg_.f32 && a_one) return "nt_rcp32(" + B + ")";
+      return A + " / " + B;
     case NT_NEG: return "-" + A;
     case NT_EXP: {
       // fp32 tapes under the reference's fp32 semantics take the float-result
@@ -186,7 +202,7 @@ std::string Emitter::fwd_expr(int op, const std::string& A, const std::string& B
 // Adjoint contribution of one node (ScalarReplay.java:139-165).  da/db are
 // null when that argument is inactive (no contribution emitted).
 void Emitter::emit_rule(int op, const std::string& D, const std::string& Va, const std::string& Vb,
-                        const std::string& Vi, const std::string* da, const std::string* db) {
+                        const std::string& Vi, const std::string* da, const std::string* db, bool a_one) {
   const std::string half = cfg_.f32 ? "0.5f" : "0.5";
   const std::string zero = cfg_.f32 ? "0.0f" : "0.0";
   switch (op) {
@@ -203,8 +219,22 @@ void Emitter::emit_rule(int op, const std::string& D, const std::string& Va, con
       if (db) o_.line(contrib(*db, '+', D + " * " + Va));
       break;
     case NT_DIV:
-      if (da) o_.line(contrib(*da, '+', D + " / " + Vb));
-      if (db) o_.line(contrib(*db, '-', D + " * " + Vi + " / " + Vb));
+      if (!cfg_.f32) {  // the interpreter's order, so the host build keeps its bits
+        if (da) o_.line(contrib(*da, '+', D + " / " + Vb));
+        if (db) o_.line(contrib(*db, '-', D + " * " + Vi + " / " + Vb));
+      } else if (a_one && db && !da) {
+        // z = 1 / b, dz/db = -z / b = -z^2 to within the reciprocal's
+        // rounding (2^-24 relative): no division in the reverse sweep, whose
+        // tiny adjoint quotients sent the IEEE division down its slow path.
+        // The products are rounded as written (never fused into the update),
+        // so every kernel built from the tape gives the same bits.
+        o_.line(contrib(*db, '-', "nt_fmul_rn(nt_fmul_rn(" + D + ", " + Vi + "), " + Vi + ")"));
+      } else {
+        // One quotient t = D / b serves both arguments: a += t, b -= t z
+        // (the compiler evaluates the repeated D / b once).
+        if (da) o_.line(contrib(*da, '+', D + " / " + Vb));
+        if (db) o_.line(contrib(*db, '-', "nt_fmul_rn(" + D + " / " + Vb + ", " + Vi + ")"));
+      }
       break;
     case NT_NEG:
       if (da) o_.line(contrib(*da, '-', D));
@@ -275,7 +305,8 @@ void Emitter::emit_straight_forward(int32_t lo, int32_t hi) {
     }
     const std::string A = nargs(op) >= 1 ? val_outside(t_.a[i]) : "";
     const std::string B = nargs(op) >= 2 ? val_outside(t_.b[i]) : "";
-    o_.line("const " + real_t + " " + vi + " = " + fwd_expr(op, A, B, t_.c[i], t_.a[i]) + ";");
+    o_.line("const " + real_t + " " + vi + " = " +
+            fwd_expr(op, A, B, t_.c[i], t_.a[i], nargs(op) >= 1 && node_is_one(t_.a[i])) + ";");
   }
 }
 
@@ -289,7 +320,7 @@ void Emitter::emit_straight_reverse(int32_t lo, int32_t hi) {
     const std::string Va = val_outside(a), Vb = b >= 0 ? val_outside(b) : "", Vi = "v" + std::to_string(i);
     std::string da = adj_outside(a), db = b >= 0 ? adj_outside(b) : "";
     const bool aa = active_outside(a), ab = b >= 0 && active_outside(b);
-    emit_rule(op, D, Va, Vb, Vi, aa ? &da : nullptr, ab ? &db : nullptr);
+    emit_rule(op, D, Va, Vb, Vi, aa ? &da : nullptr, ab ? &db : nullptr, node_is_one(a));
   }
 }
 
@@ -374,7 +405,7 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     if (bn.op == NT_CONST && bn.cslot >= 0)
       o_.line(name(j) + " = NT_CTAB(" + unit + ", " + std::to_string(bn.cslot) + ");");
     else
-      o_.line(name(j) + " = " + fwd_expr(bn.op, A, B, bn.c, -1) + ";");
+      o_.line(name(j) + " = " + fwd_expr(bn.op, A, B, bn.c, -1, nargs(bn.op) >= 1 && ref_is_one(bn.ra)) + ";");
     exp_fn_ = "NT_EXP64(";
     emitted[j] = 1;
   }
@@ -441,7 +472,8 @@ void Emitter::emit_body_reverse(int g) {
     std::string db = nargs(bn.op) == 2 ? adj(bn.rb, &ab) : "";
     const std::string Va = val(bn.ra), Vb = nargs(bn.op) == 2 ? val(bn.rb) : "";
     const std::string Vi = "r" + G + "_" + std::to_string(j);
-    emit_rule(bn.op, "b" + std::to_string(j), Va, Vb, Vi, aa ? &da : nullptr, ab ? &db : nullptr);
+    emit_rule(bn.op, "b" + std::to_string(j), Va, Vb, Vi, aa ? &da : nullptr, ab ? &db : nullptr,
+              ref_is_one(bn.ra));
   }
   for (int32_t k : lp_.carries)
     if (lp_.body[k].active) o_.line("cd" + std::to_string(k) + " = n" + std::to_string(k) + ";");
@@ -603,7 +635,8 @@ void Emitter::emit_shared_gather() {
     const int op = t_.op[i];
     const std::string A = nargs(op) >= 1 ? val_outside(t_.a[i]) : "";
     const std::string B = nargs(op) >= 2 ? val_outside(t_.b[i]) : "";
-    o_.line("const real v" + std::to_string(i) + " = " + fwd_expr(op, A, B, t_.c[i], t_.a[i]) + ";");
+    o_.line("const real v" + std::to_string(i) + " = " +
+            fwd_expr(op, A, B, t_.c[i], t_.a[i], nargs(op) >= 1 && node_is_one(t_.a[i])) + ";");
   }
   exp_fn_ = saved;
   o_.open("if (threadIdx.x == 0) {");

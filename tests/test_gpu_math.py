@@ -106,3 +106,29 @@ def test_box_muller_legs(dev):
     th = (TWO_PI * u2).astype(LD)
     assert np.max(_ulps(c, r * np.cos(th), 2.0 ** -52)) <= 3.0
     assert np.max(_ulps(s, r * np.sin(th), 2.0 ** -52)) <= 3.0
+
+
+def test_float_result_box_muller_legs(dev):
+    """The fp32 tapes' Box-Muller (which 6) against the fp64 legs narrowed to
+    float: the same float except where the double value lies within about
+    2^-40 of a float rounding boundary, and never more than one float ulp
+    away; both within one float ulp of the long-double legs."""
+    w = _words(2_000_000, 7)
+    w = w[: len(w) // 2 * 2]
+    c64, s64 = _lib.math_eval(dev, 5, words=w)
+    c32, s32 = _lib.math_eval(dev, 6, words=w)
+    for got, want in ((c32, c64), (s32, s64)):
+        narrowed = want.astype(np.float32)
+        assert np.all(got == got.astype(np.float32))  # a float, widened
+        diff = got.astype(np.float32) != narrowed
+        print(f"float-result legs differing from the narrowed fp64 legs: {int(diff.sum())} of {len(got)}")
+        assert diff.sum() <= len(got) * 2.0 ** -12
+        gap = np.abs(got[diff] - narrowed[diff].astype(np.float64))
+        assert np.all(gap <= np.spacing(np.abs(narrowed[diff])).astype(np.float64) * 1.0001)
+    u1, u2 = _u(w[0::2]), _u(w[1::2])
+    r = np.sqrt(-2.0 * np.log(u1.astype(LD)))
+    th = (TWO_PI * u2).astype(LD)
+    for got, want in ((c32, r * np.cos(th)), (s32, r * np.sin(th))):
+        f = np.asarray(want, dtype=np.float64).astype(np.float32)
+        ulp32 = np.maximum(np.spacing(np.abs(f)).astype(np.float64), 2.0 ** -149)
+        assert np.max(np.abs(got.astype(LD) - want) / ulp32) <= 1.0

@@ -426,11 +426,14 @@ def test_cva_config5_fp64(engine, oracle_mod):
 def test_markets_equal_separate_replays(engine, oracle_mod, make, base, f32):
     """nt_replay_markets: each market's sums equal a plain replay under that
     market's inputs (same draws, per-thread order and block-order reduction).
-    The multi-market kernel recomputes the transcendentals the plain kernel
-    tapes, and the compiler may fuse a multiply-add differently there, so the
-    bound is the rounding of that: 1e-13 in fp64, 1e-6 in fp32 (the host build,
-    without contraction, is bit-exact: test_markets_host.py).  The first market
-    also matches the oracle."""
+    The multi-market kernel is compiled separately and the compiler may fuse a
+    multiply-add differently there, so the bound is the rounding of that (the
+    host build, without contraction, is bit-exact: test_markets_host.py):
+    1e-13 relative in fp64; in fp32, 1e-6 relative or 1e-6 of the sum of the
+    terms' magnitudes, sum |x_i| from the oracle, whichever is larger -- the
+    barrier's rho adds per-path terms of both signs (|sum x| is 0.09 of
+    sum |x| under the 1.1 x spot market), so its float rounding differences
+    do not shrink with the sum.  The first market also matches the oracle."""
     tape = make()
     base = list(tape.recordedInputs()) if base is None else base
     markets = [list(base)]
@@ -444,7 +447,13 @@ def test_markets_equal_separate_replays(engine, oracle_mod, make, base, f32):
         for m, x in enumerate(markets):
             ex.setInputs(x)
             want, _ = ex.replay_sums(paths, off, seed)
-            np.testing.assert_allclose(got[m], want, rtol=1e-6 if f32 else 1e-13, atol=0, err_msg=f"market {m}")
+            if f32:
+                _, scale = _oracle(oracle_mod, tape, x, paths, off, seed, f32=True)
+                err = np.abs(got[m] - want)
+                print(f"market {m}: fp32 markets vs plain, relative {err / np.abs(want)}, of sum |x| {err / scale}")
+                assert np.all(err <= 1e-6 * np.maximum(np.abs(want), scale)), f"market {m}"
+            else:
+                np.testing.assert_allclose(got[m], want, rtol=1e-13, atol=0, err_msg=f"market {m}")
     if not f32:
         want, scale = _oracle(oracle_mod, tape, markets[0], paths, off, seed)
         _assert_parity(got[0], want, scale)
