@@ -73,11 +73,12 @@ class Workload:
         return "f32" if self.f32 else "f64"
 
 
-CONFIG2_PARITY = ("fp32 kernel under the reference's fp32 semantics; at 20,000,000 scenarios its price is 1.1e-5 and its "
-                  "Greeks up to 2.6e-5 (rho) off the fp64 oracle, so the stated 1e-5 bound does NOT hold -- nor for "
-                  "the reference's own fp32 evaluation (price 1.1e-5, rho 3.4e-5), the 1 - survival term loses those "
-                  "digits; the kernel is at least as close to the fp64 oracle as the fp32 oracle is and within 1e-5 "
-                  "of the fp32 oracle (tests/test_gpu_parity.py::test_config2_full_size_against_both_oracles)")
+CONFIG2_PARITY = ("fp32 kernel under the reference's fp32 semantics (every node rounded on its own, no fused "
+                  "multiply-add); at 20,000,000 scenarios it reproduces the fp32 oracle to 5e-10 on every channel, "
+                  "and like it sits 1.1e-5 (price) and up to 3.4e-5 (rho) off the fp64 oracle, so the stated 1e-5 "
+                  "bound does NOT hold -- for no fp32 evaluation of this tape, the reference's own included: the "
+                  "1 - survival term loses those digits "
+                  "(tests/test_gpu_parity.py::test_config2_full_size_against_both_oracles)")
 
 WORKLOADS = {w.name: w for w in [
     Workload("asian1e9", 3, lambda q: q.asian_tape(252), ATM, False, 1e9, 1 << 27, SEED, 1.0,
@@ -547,15 +548,11 @@ def run_ours(args, rank: int, world: int, local_rank: int, wl: Workload) -> None
 
 
 def _nvrtc_version() -> str:
-    """The NVRTC that compiled the replay kernels: the first libnvrtc.so.12 in
-    the process (torch's bundled copy once torch is imported, as here)."""
-    try:
-        nv = ctypes.CDLL("libnvrtc.so.12")
-        major, minor = ctypes.c_int(0), ctypes.c_int(0)
-        nv.nvrtcVersion(ctypes.byref(major), ctypes.byref(minor))
-        return f"{major.value}.{minor.value}"
-    except OSError:
-        return "unknown"
+    """The NVRTC that compiled the replay kernels (the toolkit's, loaded by
+    the engine itself whatever torch has loaded)."""
+    from nablatensor_b200 import _lib
+    major, minor, _ = _lib.nvrtc_version()
+    return f"{major}.{minor}"
 
 
 def _hbm_peak():

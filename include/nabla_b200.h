@@ -78,10 +78,13 @@ typedef struct nt_tape {
 #define NT_FLAG_SHARED_CKPT 0x2  /* keep step checkpoints in shared memory instead of (L2-resident)
                                     global memory */
 #define NT_FLAG_NO_DISK_CACHE 0x4
-#define NT_FLAG_F32_FAST 0x8     /* fp32: exp/log and Box-Muller in single precision.  By default
-                                    they are evaluated in fp64 and narrowed on store, the reference's
-                                    fp32 semantics (ScalarReplay.java:37-51) */
-#define NT_FLAG_NO_FMAD 0x10     /* no multiply-add contraction (every product rounded) */
+#define NT_FLAG_F32_FAST 0x8     /* fp32: exp/log and Box-Muller in single precision, with
+                                    multiply-add contraction.  By default they are evaluated in fp64
+                                    and narrowed on store, and no product is fused into an add: every
+                                    node is rounded on its own, the reference's fp32 semantics
+                                    (ScalarReplay.java:37-51) */
+#define NT_FLAG_NO_FMAD 0x10     /* no multiply-add contraction (every product rounded); already the
+                                    default of fp32 tapes without NT_FLAG_F32_FAST */
 #define NT_FLAG_ACC_REGS 0x20    /* no effect: the per-thread accumulators it placed were replaced by
                                     the exact per-warp accumulation; kept so old callers still compile */
 #define NT_FLAG_RECOMPUTE_ALL 0x40 /* reverse sweep recomputes every loop value from the step
@@ -255,6 +258,15 @@ int nt_emit_source(const nt_tape* tape, const nt_options* options, int32_t targe
 /* Compiles a source emitted for target 0 with NVRTC to an sm_100a cubin
  * (no GPU needed); *cubin_bytes gets the image size. */
 int nt_nvrtc_check(const char* source, size_t* cubin_bytes);
+
+/* The NVRTC the engine compiles with: its version, and (when path is not
+ * null) the library file it was loaded from, copied like nt_emit_source's
+ * text.  The engine loads the CUDA toolkit's NVRTC by path, privately, so a
+ * host that has loaded another libnvrtc.so.12 (PyTorch bundles one) does not
+ * change the kernels; NT_NVRTC_LIBRARY in the environment names another file.
+ * No GPU needed.  No counterpart in the reference (its CudaRuntime binds
+ * whatever NVRTC the JVM finds). */
+int nt_nvrtc_version(int32_t* major, int32_t* minor, char* path, size_t cap, size_t* len);
 
 /* Releases the executable (AadExecutable.close). NULL is a no-op. */
 void nt_destroy(nt_exec* exec);

@@ -100,6 +100,8 @@ SIGNATURES = {
     "nt_emit_source": ([ctypes.POINTER(NtTape), ctypes.POINTER(NtOptions), ctypes.c_int32, ctypes.c_char_p,
                         ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "nt_nvrtc_check": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "nt_nvrtc_version": ([ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), ctypes.c_char_p,
+                          ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "nt_destroy": ([ctypes.c_void_p], None),
     "nt_dist_unique_id": ([ctypes.POINTER(ctypes.c_uint8)], ctypes.c_int),
     "nt_dist_attach": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint8),
@@ -209,6 +211,15 @@ def emit_source(tape, target: int = 0, **opts) -> str:
     buf = ctypes.create_string_buffer(n.value + 1)
     check(lib().nt_emit_source(ctypes.byref(s), ctypes.byref(o), target, buf, n.value + 1, ctypes.byref(n)))
     return buf.value.decode()
+
+
+def nvrtc_version():
+    """(major, minor, library path) of the NVRTC the engine compiles with."""
+    ma, mi, n = ctypes.c_int32(0), ctypes.c_int32(0), ctypes.c_size_t(0)
+    check(lib().nt_nvrtc_version(ctypes.byref(ma), ctypes.byref(mi), None, 0, ctypes.byref(n)))
+    buf = ctypes.create_string_buffer(n.value + 1)
+    check(lib().nt_nvrtc_version(ctypes.byref(ma), ctypes.byref(mi), buf, n.value + 1, ctypes.byref(n)))
+    return ma.value, mi.value, buf.value.decode()
 
 
 def nvrtc_check(source: str) -> int:

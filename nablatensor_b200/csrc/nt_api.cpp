@@ -170,6 +170,17 @@ int nt_nvrtc_check(const char* source, size_t* cubin_bytes) {
   });
 }
 
+int nt_nvrtc_version(int32_t* major, int32_t* minor, char* path, size_t cap, size_t* len) {
+  return guarded([&] {
+    if (!major || !minor) nt::fail(NT_E_INVALID_ARG, "major / minor is null");
+    int ma = 0, mi = 0;
+    nt::nvrtc_version(&ma, &mi);
+    *major = ma;
+    *minor = mi;
+    copy_out(nt::nvrtc_path(), path, cap, len);
+  });
+}
+
 void nt_destroy(nt_exec* exec) {
   if (!exec) return;
   try {

@@ -187,6 +187,9 @@ void philox_words(int32_t device, uint64_t path0, uint32_t n_paths, uint64_t see
 
 // NVRTC: compile to an sm_100a cubin (cached in memory and on disk);
 // max_regs > 0 caps the registers per thread (--maxrregcount).
+// The NVRTC the engine compiles with (loaded by path; see nt_nvrtc.cpp).
+void nvrtc_version(int* major, int* minor);
+std::string nvrtc_path();
 std::vector<char> nvrtc_compile(const std::string& source, const std::string& arch, bool use_disk_cache,
                                 double* seconds, bool fmad = true, int max_regs = 0);
 

@@ -213,3 +213,25 @@ def test_a_missing_library_fails_loudly_and_the_engine_reports_unavailable(monke
     with pytest.raises(RuntimeError, match="is missing"):
         _lib.lib()
     assert CudaAadEngine(0).isAvailable() is False
+
+
+def test_the_engine_compiles_with_the_toolkit_nvrtc_whatever_the_host_loaded_first():
+    """The engine loads the CUDA toolkit's NVRTC privately, by path.  A host
+    that has already loaded another libnvrtc.so.12 -- torch imports its own
+    bundled copy -- must not change the compiler, since two NVRTC versions may
+    fuse a multiply-add differently and so change an fp32 kernel's sums."""
+    import subprocess
+    import sys
+    probe = ("import ctypes, sys\n"
+             "if sys.argv[1] == 'torch-first':\n"
+             "    import torch  # noqa: F401  (loads its own libnvrtc.so.12)\n"
+             "from nablatensor_b200 import _lib\n"
+             "print('%d.%d %s' % _lib.nvrtc_version())\n")
+    env = dict(os.environ, PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    env.pop("NT_NVRTC_LIBRARY", None)
+    seen = [subprocess.run([sys.executable, "-c", probe, mode], capture_output=True, text=True, env=env,
+                           timeout=300, check=True).stdout.strip() for mode in ("alone", "torch-first")]
+    assert seen[0] == seen[1], seen
+    version, path = seen[0].split(" ", 1)
+    assert os.path.isabs(path) and "libnvrtc.so" in path, path
+    assert "site-packages" not in path, path
