@@ -394,9 +394,11 @@ int nt_fma_peak_sustained(int32_t device, int32_t fp64, int32_t millis, double* 
  *            word pair (words[2i], words[2i+1])
  *   which 6: the same legs from the float-result routines of fp32 tapes,
  *            as floats widened to double
- * words is read for which 0, 1 (n words), 5 and 6 (2n words), x for 2, 3 and
- * 4; out1 is written for 1, 5 and 6.  n is in [1, 2^24].  Test support; no
- * counterpart in the reference. */
+ *   which 7: out0[i] = the first-pass exp of a taped loop value at x[i],
+ *            out1[i] = 1 where it records the argument for the redo pass
+ * words is read for which 0, 1 (n words), 5 and 6 (2n words), x for 2, 3, 4
+ * and 7; out1 is written for 1, 5, 6 and 7.  n is in [1, 2^24].  Test
+ * support; no counterpart in the reference. */
 int nt_math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x, double* out0,
                  double* out1);
 

@@ -126,14 +126,14 @@ SIGNATURES = {
 
 def math_eval(device: int, which: int, words=None, x=None):
     """nt_math_eval: one of the replay's fp64 routines on the device over the
-    given generator words (which 0, 1, 5, 6) or arguments (2, 3, 4).  Returns
-    out0, or (out0, out1) for which 1, 5 and 6."""
+    given generator words (which 0, 1, 5, 6) or arguments (2, 3, 4, 7).
+    Returns out0, or (out0, out1) for which 1, 5, 6 and 7."""
     import numpy as np
     w = None if words is None else np.ascontiguousarray(words, dtype=np.uint32)
     a = None if x is None else np.ascontiguousarray(x, dtype=np.float64)
     n = (len(w) // 2 if which in (5, 6) else len(w)) if w is not None else len(a)
     out0 = np.empty(n, dtype=np.float64)
-    out1 = np.empty(n, dtype=np.float64) if which in (1, 5, 6) else None
+    out1 = np.empty(n, dtype=np.float64) if which in (1, 5, 6, 7) else None
     check(lib().nt_math_eval(device, which, n,
                              None if w is None else w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
                              None if a is None else a.ctypes.data_as(_f64p),

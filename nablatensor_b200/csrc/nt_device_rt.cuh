@@ -397,6 +397,33 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
   wide |= !(fabs(x) <= 0.125);
   return nt_exp_small(x);
 }
+
+/* The forward loop's first-pass form of an exp whose value is taped: the
+ * reduction and polynomial of nt_exp_cw, without its clamp, NaN select and
+ * two-step scaling.  For |x| <= 700 the result p 2^k is a normal double, so
+ * adding k to p's exponent gives nt_exp_cw's bits; any other argument (NaN
+ * included) is recorded in `wide`, and the warp's redo pass evaluates the
+ * whole loop again with nt_exp_cw. */
+NT_FN double nt_exp_cw_fast_flag(double x, bool& wide) {
+  wide |= !(fabs(x) <= 700.0);
+  const double kt = fma(x, 0x1.71547652b82fep+0 /* 1/ln2 */, 0x1.8p52);
+  const double kd = kt - 0x1.8p52;
+  const int k = (int)nt_loword(kt);
+  double r = fma(kd, -0x1.62e42fefa3800p-1 /* ln2 hi */, x);
+  r = fma(kd, -0x1.ef35793c76730p-45 /* ln2 lo */, r);
+  double q = NT_EXPW_C9;
+  q = fma(q, r, NT_EXPW_C8);
+  q = fma(q, r, NT_EXPW_C7);
+  q = fma(q, r, NT_EXPW_C6);
+  q = fma(q, r, NT_EXPW_C5);
+  q = fma(q, r, NT_EXPW_C4);
+  q = fma(q, r, NT_EXPW_C3);
+  q = fma(q, r, NT_EXPW_C2);
+  q = fma(q, r, NT_EXPW_C1);
+  q = fma(q, r, NT_EXPW_C0);
+  const double p = fma(fma(q, r, 1.0), r, 1.0);
+  return nt_from_words(nt_hiword(p) + (int)((unsigned)k << 20), nt_loword(p));
+}
 #endif
 
 /* EXP nodes of fp64 tapes: the dedicated routine on the device (the emitted
@@ -406,11 +433,14 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
  * loop's form for an exp the reverse sweep recomputes (the bare series, wide
  * arguments recorded in nt_wide), NT_EXP64W the redo pass's (full range,
  * recording too); NT_EXP64_SERIES is the recompute once the forward sweep has
- * shown every argument of the warp in the series range.  NT_EXPF32... are the
- * same four forms for fp32 tapes under the reference's fp32 semantics, with
- * float arguments and results (nt_exp_f32, nt_exp_f32s). */
+ * shown every argument of the warp in the series range; NT_EXP64T is the
+ * forward loop's first-pass form for a taped exp (full range up to |x| = 700,
+ * larger arguments recorded for the redo pass).  NT_EXPF32... are the four
+ * forms for fp32 tapes under the reference's fp32 semantics, with float
+ * arguments and results (nt_exp_f32, nt_exp_f32s). */
 #ifdef NT_HOST
 #define NT_EXP64(x) exp(x)
+#define NT_EXP64T(x) exp(x)
 #define NT_EXP64W(x) exp(x)
 #define NT_EXP64F(x) exp(x)
 #define NT_EXP64_SERIES(x) exp(x)
@@ -420,6 +450,7 @@ NT_FN double nt_exp_series_flag(double x, bool& wide) {
 #define NT_EXPF32_SERIES(x) ((float)exp((double)(x)))
 #else
 #define NT_EXP64(x) nt_exp_cw(x)
+#define NT_EXP64T(x) nt_exp_cw_fast_flag((x), nt_wide)
 #define NT_EXP64W(x) nt_exp_cw_flag((x), nt_wide)
 #define NT_EXP64F(x) nt_exp_series_flag((x), nt_wide)
 #define NT_EXP64_SERIES(x) nt_exp_small(x)

@@ -402,6 +402,7 @@ void Emitter::emit_body_forward(const std::string& pre, const std::string& unit,
     // forward sweep; the recompute itself takes the series when none was.
     if (recompute) exp_fn_ = series_exp_ ? "NT_EXP64_SERIES(" : "NT_EXP64(";
     else if (lp_.recompute[j] && lp_.tape_slot[j] < 0) exp_fn_ = fwd_fast_ ? "NT_EXP64F(" : "NT_EXP64W(";
+    else if (fwd_fast_ && !cfg_.f32) exp_fn_ = "NT_EXP64T(";
     if (bn.op == NT_CONST && bn.cslot >= 0)
       o_.line(name(j) + " = NT_CTAB(" + unit + ", " + std::to_string(bn.cslot) + ");");
     else
@@ -720,13 +721,16 @@ void Emitter::emit_scenario() {
       o_.close();
     };
     // Exps the reverse sweep recomputes run in the forward loop as the bare
-    // series, recording wide arguments; a warp that recorded one runs the
-    // loop again from its initial carries with the full-range routine (which
-    // rewrites the tape and the checkpoints).  GBM steps never take the redo.
+    // series, recording wide arguments, and fp64 exps whose values are taped
+    // skip the full-range routine's clamp and two-step scaling up to |x| =
+    // 700; a warp that recorded a wide argument runs the loop again from its
+    // initial carries with the full-range routine (which rewrites the tape
+    // and the checkpoints).  GBM steps and bond prices never take the redo.
     bool fast_exp = false;
     if (cfg_.target == 0 && (!cfg_.f32 || cfg_.wide32))
       for (int32_t j = 0; j < L; ++j)
-        fast_exp |= lp_.body[j].op == NT_EXP && lp_.recompute[j] && lp_.tape_slot[j] < 0;
+        fast_exp |= lp_.body[j].op == NT_EXP &&
+                    ((lp_.recompute[j] && lp_.tape_slot[j] < 0) || (!cfg_.f32 && lp_.tape_slot[j] >= 0));
     auto guarded_loop = [&]() {
       if (!fast_exp) {
         forward_loop();

@@ -84,6 +84,12 @@ __global__ void math_eval_kernel(int which, long long n, const unsigned* words, 
     case 3: out0[i] = nt_exp_small(x[i]); break;
     case 4: out0[i] = nt_exp_cw(x[i]); break;
     case 5: nt_bm64_words(words[2 * i], words[2 * i + 1], &out0[i], &out1[i]); break;
+    case 7: {
+      bool wide = false;
+      out0[i] = nt_exp_cw_fast_flag(x[i], wide);
+      out1[i] = wide ? 1.0 : 0.0;
+      break;
+    }
     case 6: {
       float c, sn;
       nt_bm64f_words(words[2 * i], words[2 * i + 1], &c, &sn);
@@ -101,11 +107,11 @@ namespace nt {
 
 void math_eval(int32_t device, int32_t which, int64_t n, const uint32_t* words, const double* x, double* out0,
                double* out1) {
-  if (which < 0 || which > 6) fail(NT_E_INVALID_ARG, "which must be in [0, 6]");
+  if (which < 0 || which > 7) fail(NT_E_INVALID_ARG, "which must be in [0, 7]");
   if (n < 1 || n > (1ll << 24)) fail(NT_E_INVALID_ARG, "n must be in [1, 2^24]");
-  const bool use_words = which == 0 || which == 1 || which >= 5;
+  const bool use_words = which == 0 || which == 1 || which == 5 || which == 6;
   const bool two_out = which == 1 || which >= 5;
-  const int64_t n_words = which >= 5 ? 2 * n : n;
+  const int64_t n_words = which == 5 || which == 6 ? 2 * n : n;
   if (!out0 || (two_out && !out1) || (use_words && !words) || (!use_words && !x))
     fail(NT_E_INVALID_ARG, "a required array is null");
   cuda_check(cudaSetDevice(device), "cudaSetDevice");

@@ -180,7 +180,7 @@ def test_math_eval_rejects_bad_arguments_before_touching_a_device(ntlib):
     x = np.zeros(4)
     p = out.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
     xp = x.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
-    assert L.nt_math_eval(0, 7, 4, None, xp, p, p) == _lib.NT_E_INVALID_ARG  # unknown routine
+    assert L.nt_math_eval(0, 8, 4, None, xp, p, p) == _lib.NT_E_INVALID_ARG  # unknown routine
     assert L.nt_math_eval(0, 2, 0, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # n < 1
     assert L.nt_math_eval(0, 2, (1 << 24) + 1, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # n > 2^24
     assert L.nt_math_eval(0, 0, 4, None, xp, p, None) == _lib.NT_E_INVALID_ARG  # words needed

@@ -97,6 +97,23 @@ def test_full_range_exp(dev):
     assert np.isinf(s[4]) and s[5] == 0.0 and np.isnan(s[6])
 
 
+def test_first_pass_exp_of_taped_values(dev):
+    """The forward loop's first-pass exp of a taped value (which 7) gives the
+    full-range routine's bits wherever it does not flag the argument
+    (|x| <= 700), and flags every other argument, NaN and infinities included,
+    so that the warp's redo pass evaluates it with the full-range routine."""
+    rng = np.random.default_rng(8)
+    x = np.concatenate([rng.uniform(-700.0, 700.0, 1_000_000), rng.uniform(-1.0, 1.0, 500_000),
+                        np.array([700.0, -700.0, 0.0, -0.0, 1e-300, -1e-300])])
+    got, wide = _lib.math_eval(dev, 7, x=x)
+    full = _lib.math_eval(dev, 4, x=x)
+    assert np.all(wide == 0.0)
+    assert np.array_equal(got.view(np.uint64), full.view(np.uint64))
+    out = np.array([700.5, -700.5, 710.0, -746.0, 1e300, -1e300, np.inf, -np.inf, np.nan])
+    _, wide = _lib.math_eval(dev, 7, x=out)
+    assert np.all(wide == 1.0)
+
+
 def test_box_muller_legs(dev):
     w = _words(2_000_000, 6)
     w = w[: len(w) // 2 * 2]
