@@ -162,3 +162,20 @@ def pow2_divisions(steps=24, tiny=2.0 ** -1000):
             acc = x.div(shared).add(shared).mul(0.25).add(v.div(tiny).mul(tiny))
         rec.output(acc)
     return AadRecorder.record(body)
+
+
+def near_overflow_exps(steps=8, s0=699.0):
+    """A loop whose taped exps (carry-dependent arguments) lie near the top of
+    the double range: exp(s) for s a random walk from s0, scaled by 1e-300 so
+    that the sums stay finite.  From s0 = 699 many lanes pass |x| = 700, where
+    the forward loop's first-pass exp records the argument and the warp redoes
+    the loop with the full-range routine; from 690 none does."""
+    def body(rec):
+        level = rec.input("s0", s0)
+        vol = rec.input("vol", 0.3)
+        acc = rec.constant(0.0)
+        for _ in range(steps):
+            level = level.add(rec.randn().mul(vol))
+            acc = acc.add(level.exp().mul(1e-300))
+        rec.output(acc)
+    return AadRecorder.record(body)

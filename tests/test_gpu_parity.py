@@ -26,7 +26,8 @@ from nablatensor_b200 import _lib, quant
 from nablatensor_b200.engine import AadOptions, CudaAadEngine, PrecisionEnum
 from oracle.oracle import FlatTape
 
-from tapes import every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, random_branching
+from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, near_overflow_exps,
+                   random_branching)
 
 pytestmark = pytest.mark.gpu
 
@@ -401,6 +402,19 @@ def test_wide_exp_arguments_take_the_guarded_redo(engine, oracle_mod, vol, steps
         got, _ = ex.replay_sums(40_000, 0x1_0000_0003, 42)
     want, scale = _oracle(oracle_mod, tape, x, 40_000, 0x1_0000_0003, 42)
     _assert_parity(got, want, scale)
+
+
+@pytest.mark.parametrize("s0", [699.0, 690.0])
+def test_taped_exps_near_overflow_take_the_redo(engine, oracle_mod, s0):
+    """Taped exps run in the forward loop's first pass without the full-range
+    routine's clamp and two-step scaling, recording any argument beyond 700.
+    From s0 = 699 many lanes pass 700 (their warps redo the loop with the
+    full-range routine); from 690 none does.  Both match the oracle."""
+    tape = near_overflow_exps(s0=s0)
+    with engine.compile(tape, FP64) as ex:
+        got, _ = ex.replay_sums(40_000, 0x1_0000_0003, 42)
+    want, scale = _oracle(oracle_mod, tape, tape.recordedInputs(), 40_000, 0x1_0000_0003, 42)
+    _assert_parity(got, want, scale, label=f"taped exps from {s0}")
 
 
 def test_cva_config5_fp64(engine, oracle_mod):
