@@ -371,6 +371,31 @@ def test_general_tapes_fp64(engine, oracle_mod, make, inputs, seed):
     _assert_parity(got, want, scale)
 
 
+@pytest.mark.parametrize("make,inputs,seed", [
+    (every_op_tape, [1.3, 0.7], 0x5EED5),
+    (lambda: named_streams(16), [100.0, 0.2], 0xC0FFEE),
+    (lambda: multi_output(40), [100.0, 0.25], 17),
+    (lambda: random_branching(24), [1.2, 0.1], 0x12345678FEDCBA98),
+    (lambda: lookback(64, True), ATM, 5),
+])
+def test_general_tapes_fp32(engine, oracle_mod, make, inputs, seed):
+    """fp32 kernels of the general tapes (every op, both DIV adjoint forms,
+    MAX/MIN ties, streams, several outputs) against the oracle's fp32 mode.
+    The kernel rounds every node on its own as the oracle does; it forms a
+    divisor's adjoint as (d / b) * z in two float roundings where the oracle
+    rounds d * z / b once from double, and its transcendentals round once
+    from about 2^-40, so a per-path value may differ by an ulp: 1e-6 of the
+    channel or of the sum of its terms' magnitudes."""
+    tape = make()
+    with engine.compile(tape, FP32) as ex:
+        ex.setInputs(inputs)
+        got, _ = ex.replay_sums(20_000, 0x1_0000_0003, seed)
+    want, scale = _oracle(oracle_mod, tape, inputs, 20_000, 0x1_0000_0003, seed, f32=True)
+    err = np.abs(got - want)
+    print("fp32 general tape vs fp32 oracle, relative:", err / np.maximum(np.abs(want), 1e-300))
+    assert np.all(err <= 1e-6 * np.maximum(np.abs(want), scale))
+
+
 def test_basket_config4_fp64(engine, oracle_mod):
     """Benchmark configuration 4: 10-asset basket, 52 weekly steps, 21 Greeks."""
     tape = quant.basket_tape()
