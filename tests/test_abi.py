@@ -235,3 +235,21 @@ def test_the_engine_compiles_with_the_toolkit_nvrtc_whatever_the_host_loaded_fir
     version, path = seen[0].split(" ", 1)
     assert os.path.isabs(path) and "libnvrtc.so" in path, path
     assert "site-packages" not in path, path
+
+
+def test_a_missing_nvrtc_is_an_error_status_not_a_crash():
+    """NT_NVRTC_LIBRARY naming a file that does not exist: compiling fails
+    with NT_E_NVRTC and a message naming the file."""
+    import subprocess
+    import sys
+    probe = ("from nablatensor_b200 import _lib, quant\n"
+             "try:\n"
+             "    _lib.nvrtc_check(_lib.emit_source(quant.asian_tape(4), 0))\n"
+             "    print('compiled')\n"
+             "except _lib.NablaError as e:\n"
+             "    print(e.code == _lib.NT_E_NVRTC, str(e))\n")
+    env = dict(os.environ, PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+               NT_NVRTC_LIBRARY="/nonexistent/libnvrtc.so.12")
+    out = subprocess.run([sys.executable, "-c", probe], capture_output=True, text=True, env=env, timeout=300,
+                         check=True).stdout
+    assert out.startswith("True") and "/nonexistent/libnvrtc.so.12" in out, out
