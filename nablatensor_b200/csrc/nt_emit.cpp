@@ -230,10 +230,11 @@ void Emitter::emit_rule(int op, const std::string& D, const std::string& Va, con
         // so every kernel built from the tape gives the same bits.
         o_.line(contrib(*db, '-', "nt_fmul_rn(nt_fmul_rn(" + D + ", " + Vi + "), " + Vi + ")"));
       } else {
-        // One quotient t = D / b serves both arguments: a += t, b -= t z
-        // (the compiler evaluates the repeated D / b once).
+        // The interpreter's partials exactly: d / b is the correctly rounded
+        // float quotient either way, and d z / b is formed in double (the
+        // product of two floats is exact there) and rounded once to float.
         if (da) o_.line(contrib(*da, '+', D + " / " + Vb));
-        if (db) o_.line(contrib(*db, '-', "nt_fmul_rn(" + D + " / " + Vb + ", " + Vi + ")"));
+        if (db) o_.line(contrib(*db, '-', "(real)((double)" + D + " * (double)" + Vi + " / (double)" + Vb + ")"));
       }
       break;
     case NT_NEG:

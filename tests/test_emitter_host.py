@@ -116,11 +116,26 @@ def test_price_only(oracle_mod):
     _run(oracle_mod, quant.asian_tape(252), ATM, 1_000, 0, 42, adjoints=False)
 
 
-def test_fp32_host_build_tracks_the_fp32_oracle(oracle_mod):
-    # fp32 evaluates each node in float; the oracle evaluates in double and
-    # rounds each stored value, so compound adjoint rules and libm's float
-    # functions differ in the last bits.
-    _run(oracle_mod, fp32_asian_50(50), [100.0, 0.2], 5_000, 0, 0xA51A17, rtol=2e-6, f32=True)
+@pytest.mark.parametrize("make,inputs", [
+    (lambda: fp32_asian_50(50), [100.0, 0.2]),
+    (every_op_tape, [1.3, 0.7]),
+    (lambda: random_branching(24), [1.2, 0.1]),
+    (lambda: lookback(64, True), ATM),
+    (lambda: named_streams(16), [100.0, 0.2]),
+])
+def test_fp32_host_build_is_bit_exact(oracle_mod, make, inputs):
+    """fp32 host builds against the oracle's fp32 mode, bit for bit: every
+    node rounded to float on its own, transcendentals in double and narrowed,
+    each adjoint partial formed as the interpreter forms it (a divisor's
+    d z / b in double, rounded once)."""
+    _run(oracle_mod, make(), inputs, 3_000, 0x1_0000_0003, 0xA51A17, f32=True)
+
+
+def test_fp32_reciprocal_adjoint_within_an_ulp_of_the_oracle(oracle_mod):
+    """The one fp32 partial formed differently: the adjoint of z = 1 / b is
+    -d z z (two float products) where the interpreter forms -d z / b in
+    double; the barrier's sums stay within 1e-7 of the fp32 oracle's."""
+    _run(oracle_mod, quant.barrier_tape(252), ATM, 3_000, 0x1_0000_0003, 42, rtol=1e-7, f32=True)
 
 
 @pytest.mark.parametrize("n,steps", [(3, 8), (4, 5)])

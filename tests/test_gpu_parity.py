@@ -379,13 +379,13 @@ def test_general_tapes_fp64(engine, oracle_mod, make, inputs, seed):
     (lambda: lookback(64, True), ATM, 5),
 ])
 def test_general_tapes_fp32(engine, oracle_mod, make, inputs, seed):
-    """fp32 kernels of the general tapes (every op, both DIV adjoint forms,
-    MAX/MIN ties, streams, several outputs) against the oracle's fp32 mode.
-    The kernel rounds every node on its own as the oracle does; it forms a
-    divisor's adjoint as (d / b) * z in two float roundings where the oracle
-    rounds d * z / b once from double, and its transcendentals round once
-    from about 2^-40, so a per-path value may differ by an ulp: 1e-6 of the
-    channel or of the sum of its terms' magnitudes."""
+    """fp32 kernels of the general tapes (every op, MAX/MIN ties, streams,
+    several outputs) against the oracle's fp32 mode.  The kernel rounds every
+    node on its own and forms every adjoint partial as the oracle does (their
+    host builds are bit-exact: test_emitter_host.py); on the device its
+    transcendentals round once from about 2^-40, so a rare per-path value may
+    differ by an ulp: 1e-6 of the channel or of the sum of its terms'
+    magnitudes."""
     tape = make()
     with engine.compile(tape, FP32) as ex:
         ex.setInputs(inputs)
