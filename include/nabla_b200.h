@@ -146,7 +146,8 @@ typedef struct nt_exec_info {
   int32_t markets_registers;   /* the multi-market kernel's, 0 until nt_replay_markets compiled it */
   int32_t markets_local_bytes;
   double compile_seconds;   /* NVRTC + module load, 0 on a cache hit */
-  double fwd_flops;         /* algorithmic flops per scenario, forward (weights in DESIGN) */
+  double fwd_flops;         /* algorithmic flops per scenario, forward: arithmetic 1, exp 29,
+                               log 44, sqrt 13, sincos 36 (nt_flops.cpp) */
   double rev_flops;         /* algorithmic flops per scenario, reverse */
   double wide_flops;        /* fp32 tapes: the part of fwd_flops evaluated in fp64 (exp, log and
                                Box-Muller under the reference's fp32 semantics); 0 for fp64 tapes */

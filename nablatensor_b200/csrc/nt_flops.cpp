@@ -5,8 +5,9 @@
 // A transcendental counts the fp64 flops (DFMA = 2, DADD = DMUL = 1) that the
 // CUDA library routine executes per call, measured once with ncu's
 // smsp__sass_thread_inst_executed_op_d{fma,add,mul}_pred_on counters on the
-// isolated probe kernels of nt_kat.cu (`bench.py --math-probes`, summary in
-// profiles/fp64_math_probes_ncu.md), less the probe's own input arithmetic.
+// isolated probe kernels of the standalone program tests/probes/math_probes.cu
+// (summary in profiles/fp64_math_probes_ncu.md), less the probe's own input
+// arithmetic.
 // The replay kernels call dedicated routines for the Box-Muller and small-
 // argument exp, which execute fewer instructions; the weights stay those of
 // the library routines, so a faster routine raises the reported fraction of
