@@ -430,7 +430,17 @@ Plan plan_tape(const Tape& t, const EmitConfig& cfg) {
       for (uint8_t k : kept) per_unit += k;
     }
     const int32_t words = cfg.f32 ? 1 : 2;
-    const int32_t auto_target = per_unit > 0 ? std::max(1, std::min(16, 64 / (per_unit * words))) : std::max(1, 8 / U);
+    // fp64 with a value tape: about 112 registers.  A light unit then runs
+    // longer segments (the 252-step Asian: 9 units where 64 registers gave 6;
+    // 156 registers, one 256-thread block per SM): the reverse sweep has more
+    // independent work per segment, and the tape in flight, half as many
+    // threads', stays in L2 -- +2.7 % in a 2^27-scenario launch, +6.6 % over
+    // 1e9 scenarios per step under the power limit (7 units, still two
+    // blocks per SM, gained 1 %).  fp32 tapes keep 64: the barrier with 6
+    // units instead of 3 fell from 5 to 2 resident blocks and ran 5 % slower.
+    const int32_t budget = (!cfg.f32 && cfg.tape) ? 112 : 64;
+    const int32_t auto_target =
+        per_unit > 0 ? std::max(1, std::min(16, budget / (per_unit * words))) : std::max(1, 8 / U);
     const int32_t target = cfg.seg_units > 0 ? cfg.seg_units : auto_target;
     int32_t G = target;
     if (units >= 2) {
