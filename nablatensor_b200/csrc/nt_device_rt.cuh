@@ -757,6 +757,38 @@ NT_FN void nt_prefetch_l2_bulk(const void* p, unsigned bytes) {
 #endif
 }
 
+/* A value tape whose whole grid's share is at most this many bytes stays in
+ * the B200's 126 MB L2 between its forward write and its reverse read (about
+ * three quarters of it, leaving room for everything else the kernel touches). */
+#define NT_L2_TAPE_BYTES (96ull << 20)
+
+#ifndef NT_HOST
+/* Drops this warp's part of ROWS tape rows from L2 without writing them back
+ * (discard.global.L2: the lines' contents become undefined).  The reverse
+ * sweep of the last output calls it once a segment's taped values are
+ * consumed: nothing reads them again before the next path's forward sweep
+ * writes them anew, so their write-back to DRAM is wasted traffic.  A warp's
+ * part of a row is 32 consecutive values at src + r * BLOCK (the warp's first
+ * value at src): 256 bytes in fp64, two 128-byte lines; 128 bytes in fp32.
+ * Every line starts on a 128-byte boundary, as the instruction needs: the
+ * tile's rows and the warps' parts are multiples of 32 * sizeof(T) bytes from
+ * a 256-byte aligned allocation. */
+template <typename T, int ROWS, int BLOCK>
+NT_FN void nt_discard_rows_l2(const T* src, unsigned lane) {
+  constexpr int kLines = 32 * (int)sizeof(T) / 128;
+  constexpr int kTotal = ROWS * kLines;
+#pragma unroll
+  for (int i = 0; i < (kTotal + 31) / 32; ++i) {
+    const int c = i * 32 + (int)lane;
+    if (c < kTotal) {
+      const int r = c / kLines, k = c % kLines;
+      const char* line = reinterpret_cast<const char*>(src + (size_t)r * BLOCK) + 128 * k;
+      asm volatile("discard.global.L2 [%0], 128;" ::"l"(line) : "memory");
+    }
+  }
+}
+#endif
+
 /* ---- java.lang.Math semantics ------------------------------------------- */
 
 NT_FN bool nt_signbit64(double x) {

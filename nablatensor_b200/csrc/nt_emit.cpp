@@ -102,6 +102,15 @@ class Emitter {
   // a launch: the CUDA kernel evaluates them once per block into shared
   // memory (nt_gvs[k * N + unit]) instead of a per-thread array per scenario.
   bool gv_shared_ = false;
+  // A light unit's value tape (the Asian's 2 KB per thread) can stay in L2
+  // while in flight, at the occupancy such kernels run: the last reverse sweep
+  // then drops each consumed segment's rows from L2 (nt_discard_rows_l2),
+  // when the kernel finds at run time that the grid's whole tape fits
+  // (nt_tape_in_l2).  Measured on the 252-step Asian over 1e9 scenarios per
+  // step: +1.1 to +1.4 %, the same bits.  Heavy units (basket, CVA) move
+  // tapes far beyond L2 and do not emit it: on the CVA book the extra code
+  // alone cost 5 %.
+  bool discard_ = false;
   std::string gv_ref(int32_t k, const std::string& unit) const {
     if (gv_shared_) return "nt_gvs[" + std::to_string(k * lp_.N) + " + " + unit + "]";
     return "nt_gv" + std::to_string(k) + "[" + unit + "]";
@@ -558,6 +567,19 @@ void Emitter::emit_reverse_for_output(int o) {
                         true, g);
     }
     for (int g = G - 1; g >= 0; --g) emit_body_reverse(g);
+    if (discard_ && o == t_.n_out() - 1) {
+      // The last output's sweep has consumed this segment's tape rows; no
+      // read follows before the next path rewrites them, so when the tape in
+      // flight fits in L2 the warp drops its part of them there instead of
+      // leaving dirty lines to be written back.  Every lane's loads of the
+      // rows are done (their values are used above, and the __syncwarp orders
+      // them before any lane's discard).
+      o_.open("if (nt_tape_in_l2) {");
+      o_.line("__syncwarp();");
+      o_.line("nt_discard_rows_l2<real, " + std::to_string(G) + " * NT_NTAPE, NT_BLOCK>(nt_tape_blk + (nt_u64)s * (" +
+              std::to_string(G) + " * NT_NTAPE * NT_BLOCK) + (threadIdx.x & ~31u), nt_lane);");
+      o_.close();
+    }
     o_.close();
     // Unit 0's carry adjoints belong to the carries' initial values.
     for (size_t c = 0; c < lp_.carries.size(); ++c) {
@@ -797,6 +819,7 @@ std::string Emitter::run() {
   const bool host = cfg_.target == 1;
   const bool mk = cfg_.markets;
   gv_shared_ = cfg_.target == 0 && !mk && gather_is_launch_invariant();
+  discard_ = cfg_.target == 0 && !mk && cfg_.adjoints && lp_.present && lp_.n_tape > 0 && p_.per_unit_regs <= 32;
   const int32_t nck_total = ckpt_values(p_);
   o_.line("// Generated by libnabla_b200 from a " + std::to_string(t_.n) + "-node tape.");
   if (host) {
@@ -918,6 +941,9 @@ std::string Emitter::run() {
             "NT_BLOCK);");
     o_.line("real* __restrict__ const nt_tape_b = nt_tape_blk + threadIdx.x;");
   }
+  if (discard_)
+    o_.line("const bool nt_tape_in_l2 = (nt_u64)gridDim.x * NT_BLOCK * NT_NLOOP * NT_NTAPE * sizeof(real) <= "
+            "NT_L2_TAPE_BYTES;");
   if (mk) {
     // Compensated per-market accumulators in a global block tile
     // [block][2 * market * NT_CH + 2k (+1)][thread of block], zeroed by the
