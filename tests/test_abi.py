@@ -204,6 +204,50 @@ def test_plan_features_compile_for_sm100a(ntlib, make, opts, target):
     assert _lib.nvrtc_check(src) > 1000
 
 
+def _segments(src):
+    m = re.search(r"step loop: (\d+) units of \d+ nodes \(\d+ steps each\), (\d+) segments of (\d+) units", src)
+    return int(m.group(1)), int(m.group(2)), int(m.group(3))
+
+
+def test_automatic_segment_lengths(ntlib):
+    """fp64 tapes with a value tape plan segments within about 112 registers,
+    the rest within 64: the Asian gets 9 units, the fp32 barrier 3, the heavy
+    basket and CVA units 1, the recompute-all Asian 6."""
+    asian = quant.asian_tape(252)
+    assert _segments(_lib.emit_source(asian)) == (126, 14, 9)
+    rc = _lib.NT_FLAG_RECOMPUTE_ALL | _lib.NT_FLAG_SHARED_CKPT
+    assert _segments(_lib.emit_source(asian, flags=rc)) == (126, 21, 6)
+    assert _segments(_lib.emit_source(quant.barrier_tape(252), precision=_lib.NT_FLOAT32)) == (126, 42, 3)
+    assert _segments(_lib.emit_source(quant.basket_tape()))[2] == 1
+    assert _segments(_lib.emit_source(quant.cva_tape()))[2] == 1
+
+
+def test_l2_discard_of_consumed_tape_rows_is_placed_safely(ntlib):
+    """discard.global.L2 of a consumed tape segment is emitted only where a
+    light unit's tape can stay in L2, under the kernel's run-time check that
+    the grid's tape fits, and only in the last output's reverse sweep: an
+    earlier output's sweep reads the same rows again."""
+    def sweeps(src):
+        return [m.start() for m in re.finditer(r"reverse sweep, output (\d+)", src)]
+
+    src = _lib.emit_source(quant.asian_tape(252))
+    assert "const bool nt_tape_in_l2 =" in src
+    # one per reverse copy (series and guarded), each inside `if (nt_tape_in_l2)`
+    assert src.count("nt_discard_rows_l2<") == 2
+    assert src.count("if (nt_tape_in_l2) {") == 2
+    two = _lib.emit_source(multi_output(40))
+    starts = sweeps(two)
+    assert len(starts) == 2
+    hits = [m.start() for m in re.finditer(r"nt_discard_rows_l2<", two)]
+    assert hits and all(h > starts[1] for h in hits)
+    # heavy units, recompute-all, the host build and the multi-market kernel: none
+    rc = _lib.NT_FLAG_RECOMPUTE_ALL | _lib.NT_FLAG_SHARED_CKPT
+    for src in (_lib.emit_source(quant.cva_tape()), _lib.emit_source(quant.basket_tape()),
+                _lib.emit_source(quant.asian_tape(252), flags=rc), _lib.emit_source(quant.asian_tape(252), target=1),
+                _lib.emit_source(quant.asian_tape(252), target=2)):
+        assert "nt_discard_rows_l2<" not in src
+
+
 def test_a_missing_library_fails_loudly_and_the_engine_reports_unavailable(monkeypatch):
     """No fallback: without libnabla_b200.so every entry raises, and the SPI's
     isAvailable() answers False without throwing (AadEngine.java:39-40)."""
