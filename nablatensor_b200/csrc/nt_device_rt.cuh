@@ -789,6 +789,12 @@ NT_FN void nt_discard_rows_l2(const T* src, unsigned lane) {
 }
 #endif
 
+#ifndef NT_HOST
+/* Component B of a vector pair (the per-unit constant table's paired loads). */
+template <int B> NT_FN double nt_pick(double2 v) { return B ? v.y : v.x; }
+template <int B> NT_FN float nt_pick(float2 v) { return B ? v.y : v.x; }
+#endif
+
 /* ---- java.lang.Math semantics ------------------------------------------- */
 
 NT_FN bool nt_signbit64(double x) {
