@@ -242,7 +242,9 @@ def test_l2_discard_of_consumed_tape_rows_is_placed_safely(ntlib):
     assert hits and all(h > starts[1] for h in hits)
     # heavy units, recompute-all, the host build and the multi-market kernel: none
     rc = _lib.NT_FLAG_RECOMPUTE_ALL | _lib.NT_FLAG_SHARED_CKPT
-    for src in (_lib.emit_source(quant.cva_tape()), _lib.emit_source(quant.basket_tape()),
+    # and the fp32 barrier, whose tape (3 KB per thread) cannot fit even at one block per SM
+    barrier = _lib.emit_source(quant.barrier_tape(252), precision=_lib.NT_FLOAT32)
+    for src in (barrier, _lib.emit_source(quant.cva_tape()), _lib.emit_source(quant.basket_tape()),
                 _lib.emit_source(quant.asian_tape(252), flags=rc), _lib.emit_source(quant.asian_tape(252), target=1),
                 _lib.emit_source(quant.asian_tape(252), target=2)):
         assert "nt_discard_rows_l2<" not in src
