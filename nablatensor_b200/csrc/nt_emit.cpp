@@ -820,9 +820,9 @@ std::string Emitter::run() {
   const bool mk = cfg_.markets;
   gv_shared_ = cfg_.target == 0 && !mk && gather_is_launch_invariant();
   // Emitted only where the tape can fit at all: one block on each of the
-  // B200's 148 SMs must stay within the run-time budget (the fp32 barrier's
-  // 256 x 3 KB x 148 = 114 MB never does, and the code alone cost it 16
-  // registers).
+  // B200's 148 SMs must stay within the run-time budget (96 MB, the device
+  // runtime's NT_L2_TAPE_BYTES; the fp32 barrier's 256 x 3 KB x 148 = 114 MB
+  // never does, and the code alone cost it 16 registers).
   discard_ = cfg_.target == 0 && !mk && cfg_.adjoints && lp_.present && lp_.n_tape > 0 && p_.per_unit_regs <= 32 &&
              (uint64_t)148 * cfg_.block * lp_.N * lp_.n_tape * (cfg_.f32 ? 4 : 8) <= (96ull << 20);
   const int32_t nck_total = ckpt_values(p_);
