@@ -27,7 +27,7 @@ from nablatensor_b200.engine import AadOptions, CudaAadEngine, PrecisionEnum
 from oracle.oracle import FlatTape
 
 from tapes import (every_op_tape, fp32_asian_50, lookback, multi_output, named_streams, near_overflow_exps,
-                   random_branching)
+                   nonuniform_asian, random_branching)
 
 pytestmark = pytest.mark.gpu
 
@@ -361,6 +361,7 @@ def test_shared_checkpoints_and_recompute_all_agree(engine):
     (lambda: lookback(64, True), ATM, 5),
     (lambda: quant.barrier_tape(252), ATM, 42),
     (lambda: quant.european_tape(1), ATM, 20260830),
+    (lambda: nonuniform_asian(60), [100.0, 100.0, 0.2, 0.03], 9),  # per-unit constants: paired table loads
 ])
 def test_general_tapes_fp64(engine, oracle_mod, make, inputs, seed):
     tape = make()
@@ -377,6 +378,7 @@ def test_general_tapes_fp64(engine, oracle_mod, make, inputs, seed):
     (lambda: multi_output(40), [100.0, 0.25], 17),
     (lambda: random_branching(24), [1.2, 0.1], 0x12345678FEDCBA98),
     (lambda: lookback(64, True), ATM, 5),
+    (lambda: nonuniform_asian(60), [100.0, 100.0, 0.2, 0.03], 9),  # per-unit constants in float pairs
 ])
 def test_general_tapes_fp32(engine, oracle_mod, make, inputs, seed):
     """fp32 kernels of the general tapes (every op, MAX/MIN ties, streams,
